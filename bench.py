@@ -1,0 +1,438 @@
+#!/usr/bin/env python
+"""DSA decode benchmark: FP8 lightning indexer (top-2048) -> sparse MLA
+attention, one decode step per "step", on N GPUs of one node.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload north_star|config4]
+
+For N > 1 launch under torchrun (one process per GPU).  The decode batch is
+sharded by request; every rank owns its own page pools and no collective runs
+inside the timed region (NCCL only gathers outputs for verification after it).
+
+Workloads (seeded synthetic data with the contest shapes):
+  north_star  64 requests per GPU, 65536-token context each (weak scaling).
+  config4     512 requests in total, context log-uniform in [4096, 131072],
+              split across the GPUs by context tokens (strong scaling).
+
+Printed (rank 0, one JSON line): whole-job algorithmic HBM GB/s (value), the
+step time, the roofline of the dominant operator, the CPU oracle baseline,
+an end-to-end figure through the public run() API with host buffers, the
+number of our kernel launches and the SM clocks seen while timing.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "flashinfer-bench-starter-kit_b200"))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+METRIC = "DSA decode µs/step + HBM GB/s (indexer+attn) at 1/2/4/8 B200 vs CPU reference"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["north_star", "config4"], default="north_star")
+    ap.add_argument("--streams", type=int, default=1, help="streams inside the captured step")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def workload_lengths(name: str, rank: int, world: int) -> tuple:
+    """(this rank's seq_lens, total requests, description)."""
+    from dsa_b200 import sharding, workloads
+
+    if name == "north_star":
+        return [65536] * 64, 64 * world, "64 requests/GPU x 65536-token context"
+    g = torch.Generator().manual_seed(4)
+    lens = workloads.log_uniform_lengths(512, 4096, 131072, g)
+    shards = sharding.shard_requests(lens, world)
+    return [lens[i] for i in shards[rank]], 512, "512 requests, context log-uniform [4096, 131072]"
+
+
+def measured_peaks() -> tuple:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(kernel: str, workload: str):
+    """Per-launch DRAM bytes from profiles/traffic.txt ("kernel workload bytes")."""
+    p = REPO / "profiles" / "traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 3 and parts[0] == kernel and parts[1] == workload:
+            try:
+                return float(parts[2])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.out = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            uid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self.cmd = ["nvidia-smi", "-i", uid, f"--query-gpu={self.FIELDS}",
+                        "--format=csv,noheader,nounits", "-lms", "100"]
+        except Exception:
+            self.cmd = None
+
+    def __enter__(self):
+        if self.cmd:
+            try:
+                self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE,
+                                             stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        if not self.out:
+            return {"unavailable": "nvidia-smi sampling failed"}
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = max(mx, float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"unavailable": "no samples"}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU side
+def cpu_oracle_sample(dec, topk_gpu, seconds: float) -> dict:
+    """Times the CPU oracle on request 0 of this rank's batch: indexer over
+    its whole context plus attention for its query token."""
+    import math
+
+    from dsa_b200 import workloads
+    from oracle import attention as oatt
+    from oracle import indexer as oix
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    ix = dec.indexer
+    L = int(ix.seq_lens[0])
+    n_pages = (L + 63) // 64
+    pages = ix.block_table[0, :n_pages].long()
+    kc = ix.k_index_cache_fp8[pages].cpu()                       # this request's pages only
+    bt = torch.arange(n_pages, dtype=torch.int32)[None]
+    q, w, sl = ix.q_index_fp8[:1].cpu(), ix.weights[:1].cpu(), ix.seq_lens[:1].cpu()
+    idx = topk_gpu[:1].long()
+    valid = idx >= 0
+    rows = torch.where(valid, idx, torch.zeros_like(idx))[0]
+    ckv = dec.ckv_cache.reshape(-1, 512)[rows].cpu()             # gathered rows, compacted
+    kpe = dec.kpe_cache.reshape(-1, 64)[rows].cpu()
+    local = torch.where(valid[0].cpu(), torch.arange(2048), torch.full((2048,), -1))[None]
+    qn, qp = dec.q_nope[:1].cpu(), dec.q_pe[:1].cpu()
+    nbytes = workloads.indexer_bytes([L]) + workloads.attention_bytes(1)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while True:
+        t0 = time.perf_counter()
+        oix.indexer_reference(q, kc, w, sl, bt)
+        oatt.attention_reference(qn, qp, ckv, kpe, local, dec.sm_scale)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(times) >= 50:
+            break
+    t = statistics.median(times)
+    del math
+    return {"value": nbytes / t / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"1 request (L={L}) indexer + its attention token, {len(times)} reps, "
+                      f"median {t * 1e3:.1f} ms"}
+
+
+def run_reference(args, rank: int, world: int) -> int:
+    """CPU oracle (the reference algorithm restated) on bounded samples."""
+    if rank != 0:
+        return 0
+    from dsa_b200 import workloads
+    from oracle import attention as oatt
+    from oracle import indexer as oix
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    lens, total_req, desc = workload_lengths(args.workload, 0, world)
+    L = lens[0]
+    dec = workloads.make_decode_inputs([L], seed=77, device="cpu")
+    ix = dec.indexer
+    nbytes = workloads.indexer_bytes([L]) + workloads.attention_bytes(1)
+    times = []
+    for k in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        topk, _ = oix.indexer_reference(ix.q_index_fp8, ix.k_index_cache_fp8, ix.weights,
+                                        ix.seq_lens, ix.block_table)
+        oatt.attention_reference(dec.q_nope, dec.q_pe, dec.ckv_cache, dec.kpe_cache, topk,
+                                 dec.sm_scale)
+        if k >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    t = sum(times) / len(times)
+    gbs = nbytes / t / 1e9
+    cores = torch.get_num_threads()
+    sample = f"1 request (L={L}) indexer + 1 attention token per step"
+    line = {
+        "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak" if args.workload == "north_star" else "strong", "vs_baseline": None,
+        "dtype": "fp32 (CPU oracle)", "data": "synthetic (seeded)", "impl": "reference",
+        "config": {"workload": args.workload, "description": desc, "global_batch": total_req,
+                   "l2": "inputs larger than L2"},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU side
+def main() -> int:
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    import torch.distributed as dist
+
+    from dsa_b200 import pipeline, workloads
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    lens, total_req, desc = workload_lengths(args.workload, rank, world)
+    dec = workloads.make_decode_inputs(lens, seed=1000 + rank, device=dev)
+    step = pipeline.DecodeStep(dec, use_graph=True, streams=args.streams)
+    ix_bytes = workloads.indexer_bytes(lens)
+    at_bytes = workloads.attention_bytes(len(lens))
+    rank_bytes = ix_bytes + at_bytes
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+
+    # ---- timed region: K whole steps (indexer graph + attention graph) ----
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    with ClockSampler(dev) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_stop = torch.cuda.Event(enable_timing=True)
+        t_start.record()
+        for k in range(K):
+            ev[k][0].record()
+            step.indexer_graph()
+            ev[k][1].record()
+            step.attention_graph()
+            ev[k][2].record()
+        t_stop.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms_total = t_start.elapsed_time(t_stop)
+    ix_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / K
+    at_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / K
+    stats = torch.tensor([ms_total, float(rank_bytes), float(len(lens))], dtype=torch.float64,
+                         device=dev)
+    if world > 1:
+        mx = stats.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = stats.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms_total, total_bytes, n_req = float(mx[0]), float(sm[1]), float(sm[2])
+    else:
+        total_bytes, n_req = float(rank_bytes), float(len(lens))
+    ms_step = ms_total / K
+    value = total_bytes / (ms_step * 1e-3) / 1e9
+
+    # ---- end to end through the public run() API with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        e2e = end_to_end(step, dec, args, world, local_rank, total_bytes)
+
+    # ---- verification gather (outside the timed region) ----
+    verified = verify(step, dec, world, dev)
+
+    if rank != 0:
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+            dist.destroy_process_group()
+        return 0
+
+    peak, peak_kind = measured_peaks()
+    ix_gbs = ix_bytes / (ix_ms * 1e-3) / 1e9
+    at_gbs = at_bytes / (at_ms * 1e-3) / 1e9
+    traffic = profiled_traffic("indexer_score_kernel", args.workload)
+    cpu = None
+    if world == 1:
+        cpu = cpu_oracle_sample(dec, step.topk, args.cpu_seconds)
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,
+        "tokens_per_s": n_req / (ms_step * 1e-3), "higher_is_better": True,
+        "scaling": "weak" if args.workload == "north_star" else "strong", "vs_baseline": None,
+        "dtype": "fp8e4m3 (indexer MMA) + bf16 (attention MMA), fp32 accumulate",
+        "data": "synthetic (seeded N(0,1), contest shapes)",
+        "config": {"workload": args.workload, "description": desc, "global_batch": total_req,
+                   "requests_rank0": len(lens), "parallelism": f"dp{world} (request sharding)",
+                   "l2": "inputs larger than L2 (553 MB FP8 K cache + 151 MB gathered rows "
+                         "per GPU), no flush", "streams": args.streams},
+        "roofline": {"bound": "hbm", "op": "indexer (score + select kernels)",
+                     "achieved": ix_gbs, "peak": peak, "unit": "GB/s", "frac": ix_gbs / peak,
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                     "traffic": traffic},
+        "breakdown": {"indexer_us": ix_ms * 1e3, "attention_us": at_ms * 1e3,
+                      "indexer_gbs": ix_gbs, "attention_gbs": at_gbs,
+                      "attention_frac": at_gbs / peak,
+                      "step_frac_of_peak": value / world / peak},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": 4 * K,
+        "clocks": clk.summary(),
+        "verified": verified,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    return 0
+
+
+def end_to_end(step, dec, args, world, local_rank, total_bytes):
+    """Same metric through indexer.run / attention.run with pinned host
+    buffers: per step H2D of the step's inputs (queries, weights, lengths,
+    block table) and D2H of its outputs (indices, attention output, lse).
+    The KV caches are resident state, as in a serving loop."""
+    import torch.distributed as dist
+
+    from dsa_b200 import attention, indexer
+
+    ix = dec.indexer
+    dev_in = [ix.q_index_fp8.view(torch.uint8), ix.weights, ix.seq_lens, ix.block_table,
+              dec.q_nope, dec.q_pe]
+    host_in = [t.cpu().pin_memory() for t in dev_in]
+    dev_out = [step.topk, step.out, step.lse]
+    host_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in dev_out]
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+    def one():
+        for h, d in zip(host_in, dev_in):
+            d.copy_(h, non_blocking=True)
+        indexer.run(ix.q_index_fp8, ix.k_index_cache_fp8, ix.weights, ix.seq_lens,
+                    ix.block_table, step.topk)
+        attention.run(dec.q_nope, dec.q_pe, dec.ckv_cache, dec.kpe_cache, step.topk,
+                      dec.sm_scale, step.out, step.lse)
+        for h, d in zip(host_out, dev_out):
+            h.copy_(d, non_blocking=True)
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([a.elapsed_time(b) / args.steps], dtype=torch.float64, device=ix.seq_lens.device)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms)
+    return {"value": total_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "dsa_b200.indexer.run + dsa_b200.attention.run (eager, ctypes -> C ABI)"}
+
+
+def verify(step, dec, world, dev):
+    """Gathers every rank's top-k rows to rank 0 (NCCL) and checks they are
+    2048 distinct slots inside the request's pages, lse finite."""
+    import torch.distributed as dist
+
+    ix = dec.indexer
+    B = ix.q_index_fp8.shape[0]
+    n_pages = (ix.seq_lens.long() + 63) // 64
+    bt = ix.block_table.long()
+    page_ok = torch.zeros(B, dtype=torch.bool, device=dev)
+    pages = step.topk.long() // 64
+    for b in range(B):
+        allowed = torch.zeros(dec.ckv_cache.shape[0], dtype=torch.bool, device=dev)
+        allowed[bt[b, : int(n_pages[b])]] = True
+        page_ok[b] = allowed[pages[b]].all()
+    distinct = torch.tensor([step.topk[b].unique().numel() == 2048 for b in range(B)], device=dev)
+    ok = torch.tensor([bool((page_ok & distinct).all()) and bool(torch.isfinite(step.lse).all())],
+                      dtype=torch.int32, device=dev)
+    if world > 1:
+        allok = [torch.zeros_like(ok) for _ in range(world)]
+        dist.all_gather(allok, ok)
+        return all(bool(x.item()) for x in allok)
+    return bool(ok.item())
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,598 @@
+// attention.cu -- DSA sparse MLA attention (decode) for sm_100a.
+//
+// Replaces dsa_sparse_attention / run() of dsa_attention/solution/triton/kernel.py.
+// The reference gathers the selected bf16 rows into an fp32 [T, 2048, 576]
+// HBM buffer and runs two cuBLAS fp32 batched GEMMs around a softmax kernel
+// (kernel.py:184-217).  Here each gathered row crosses HBM exactly once, as
+// bf16, straight into shared memory:
+//
+//   attention_kernel (persistent, one CTA per SM).  The work list is
+//   T x 32 tiles of 64 selected rows; CTA c takes the contiguous slice
+//   [c*U/G, (c+1)*U/G) ("stream-K"), so every SM streams the same number of
+//   rows whatever T is.  Roles:
+//     warp 0     producer: reads 64 slot ids, TMA tile::gather4 of the rows'
+//                ckv (8 x 128-byte chunks) and kpe (1 chunk) into a 2-deep
+//                ring with 128-byte swizzle; q_nope/q_pe of the token by
+//                2-D TMA when the token changes.
+//     warp 1     MMA issuer (tcgen05, bf16, fp32 accumulators in TMEM):
+//                  S^T[64 rows, 16 heads]  = K[64, 576] . Q[16, 576]^T
+//                  (M = 64, N = 16, 36 x K16), then after the softmax
+//                  O^T[512, 16] += V^T[512, 64] . P^T[64, 16]
+//                  (4 x M = 128, N = 16, 4 x K16); V^T is the same shared
+//                  memory as the ckv chunks, read MN-major.
+//     warps 2-5  online softmax in base 2 with lazy rescaling (the running
+//                max is only moved when a tile exceeds it by more than 8,
+//                so O in TMEM is rarely touched), P^T written as bf16.
+//   A token fully covered by one CTA is normalised and written directly;
+//   otherwise the CTA writes (O, m, l) partials.
+//
+//   attention_combine_kernel merges the partials of split tokens:
+//   lse = log2 sum_i l_i 2^(m_i - M) + M, out = sum_i O_i 2^(m_i - M) / l.
+#include <cuda_bf16.h>
+
+#include <cmath>
+#include <mutex>
+
+#include "host.h"
+#include "ptx.cuh"
+
+namespace dsa {
+namespace attn {
+
+constexpr int kHeads = DSA_ATTN_HEADS;           // 16
+constexpr int kCkv = DSA_CKV_DIM;                // 512
+constexpr int kKpe = DSA_KPE_DIM;                // 64
+constexpr int kTopK = DSA_TOPK;                  // 2048
+constexpr int kRows = 64;                        // selected rows per tile
+constexpr int kTilesPerTok = kTopK / kRows;      // 32
+constexpr int kChunks = 9;                       // 8 ckv + 1 kpe chunks of 128 B
+constexpr int kChunkBytes = kRows * 128;         // 8192
+constexpr int kStageBytes = kChunks * kChunkBytes;  // 73728
+constexpr int kQChunkBytes = kHeads * 128;       // 2048
+constexpr int kQBytes = kChunks * kQChunkBytes;  // 18432
+constexpr int kPBytes = kHeads * kRows * 2;      // 2048
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 256;
+constexpr uint32_t kColO = 0;    // O^T buffers at [0,64) and [64,128): 4 blocks x 16 heads
+constexpr uint32_t kColS = 128;  // S^T buffers at [128,144) and [144,160)
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: factor 256
+constexpr int kMaxTokens = (1 << 30) / (kTopK / kRows) / kHeads;
+
+// bf16 x bf16 -> f32.  Logits: A = K rows (K-major), B = Q (K-major), M64 N16.
+constexpr uint32_t kIdescS = idesc_make(1, 1, false, false, 64, 16);
+// PV: A = V^T (MN-major view of the ckv chunks), B = P^T (K-major), M128 N16.
+constexpr uint32_t kIdescO = idesc_make(1, 1, true, false, 128, 16);
+
+constexpr int kOffStage = 0;
+constexpr int kOffQ = kOffStage + 2 * kStageBytes;   // 147456
+constexpr int kOffP = kOffQ + 2 * kQBytes;           // 184320
+constexpr int kOffSx = kOffP + 2 * kPBytes;          // 188416
+constexpr int kOffBar = kOffSx + kHeads * kRows * 4; // 192512
+constexpr int kOffMisc = kOffBar + 256;
+constexpr int kSmemBytes = 1024 + kOffMisc + 256;
+static_assert(19 * 8 <= 256, "barrier area");
+
+struct Params {
+  const int32_t* indices;
+  __nv_bfloat16* out;
+  float* lse;
+  float* part_o;   // [records][16][512]
+  float* part_ml;  // [records][16][2]
+  unsigned int* status;
+  int64_t num_slots;
+  int num_tokens;
+  int kmax;        // partial records per CTA
+  float scale_log2;
+};
+
+// Which tokens / records a CTA covers, shared by both kernels.
+__host__ __device__ inline int64_t unit_start(int64_t total, int c, int grid) {
+  return total * c / grid;
+}
+
+__device__ __forceinline__ int sanitize_slot(int v, int64_t num_slots, unsigned int* status) {
+  if (v < 0 || v >= num_slots) {
+    if (v != -1) atomicOr(status, DSA_DEV_BAD_INDEX);
+    return 0;
+  }
+  return v;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
+                 const __grid_constant__ CUtensorMap kpe_map,
+                 const __grid_constant__ CUtensorMap qn_map,
+                 const __grid_constant__ CUtensorMap qp_map, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stage_mem = smem + kOffStage;
+  uint8_t* q_mem = smem + kOffQ;
+  uint8_t* p_mem = smem + kOffP;
+  float* sx = reinterpret_cast<float*>(smem + kOffSx);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = bars + 2;
+  uint64_t* q_full = bars + 4;
+  uint64_t* q_empty = bars + 6;
+  uint64_t* s_full = bars + 8;
+  uint64_t* s_empty = bars + 10;
+  uint64_t* p_full = bars + 12;
+  uint64_t* p_empty = bars + 14;
+  uint64_t* o_empty = bars + 16;
+  uint64_t* drain = bars + 18;
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  int* abort_flag = reinterpret_cast<int*>(smem + kOffMisc + 4);
+  int* rescale_flag = reinterpret_cast<int*>(smem + kOffMisc + 8);
+  float* alpha_smem = reinterpret_cast<float*>(smem + kOffMisc + 64);   // 16
+  float* ml_smem = reinterpret_cast<float*>(smem + kOffMisc + 128);     // 16 x (m, l)
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1);
+      mbar_init(&q_full[s], 1);  mbar_init(&q_empty[s], 1);
+      mbar_init(&s_full[s], 1);  mbar_init(&s_empty[s], 128);
+      mbar_init(&p_full[s], 1);  mbar_init(&p_empty[s], 1);
+      mbar_init(&o_empty[s], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *rescale_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensor_map(&ckv_map); prefetch_tensor_map(&kpe_map);
+    prefetch_tensor_map(&qn_map);  prefetch_tensor_map(&qp_map);
+  }
+  if (warp == 1) tmem_alloc(tmem_base_smem, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem_base = *tmem_base_smem;
+  const int64_t total = static_cast<int64_t>(p.num_tokens) * kTilesPerTok;
+  const int64_t u0 = unit_start(total, blockIdx.x, gridDim.x);
+  const int64_t u1 = unit_start(total, blockIdx.x + 1, gridDim.x);
+  const int n = static_cast<int>(u1 - u0);
+  const int t_first = static_cast<int>(u0 / kTilesPerTok);
+  const WaitCtx wctx{abort_flag, p.status};
+
+  if (warp == 0) {
+    // ------------------------------------------------------ producer warp
+    const uint64_t policy = make_policy_evict_first();
+    int nq = 0, i = 0;
+    for (; i < n; ++i) {
+      const int64_t u = u0 + i;
+      const int t = static_cast<int>(u / kTilesPerTok);
+      const int tile = static_cast<int>(u % kTilesPerTok);
+      if (i == 0 || tile == 0) {
+        const int slot = nq & 1;
+        int ok = 1;
+        if (lane == 0) {
+          ok = mbar_wait(&q_empty[slot], ((nq >> 1) & 1) ^ 1, wctx);
+          if (ok) {
+            mbar_arrive_expect_tx(&q_full[slot], kQBytes);
+            uint8_t* q = q_mem + slot * kQBytes;
+            for (int c = 0; c < 8; ++c)
+              tma_load_2d(q + c * kQChunkBytes, &qn_map, &q_full[slot], c * 64, t * kHeads);
+            tma_load_2d(q + 8 * kQChunkBytes, &qp_map, &q_full[slot], 0, t * kHeads);
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        ++nq;
+      }
+      const int s = i & 1;
+      const int32_t* idx_row = p.indices + static_cast<int64_t>(t) * kTopK + tile * kRows;
+      const int v0 = sanitize_slot(__ldg(idx_row + 2 * lane), p.num_slots, p.status);
+      const int v1 = sanitize_slot(__ldg(idx_row + 2 * lane + 1), p.num_slots, p.status);
+      int ok = 1;
+      if (lane == 0) {
+        ok = mbar_wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, wctx);
+        if (ok) mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const int src = 2 * (lane & 15);
+      const int r0 = __shfl_sync(0xffffffffu, v0, src);
+      const int r1 = __shfl_sync(0xffffffffu, v1, src);
+      const int r2 = __shfl_sync(0xffffffffu, v0, src + 1);
+      const int r3 = __shfl_sync(0xffffffffu, v1, src + 1);
+      if (lane < 16) {
+        uint8_t* dst = stage_mem + s * kStageBytes + lane * 512;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          tma_gather4(dst + c * kChunkBytes, &ckv_map, &kv_full[s], c * 64, r0, r1, r2, r3, policy);
+        tma_gather4(dst + 8 * kChunkBytes, &kpe_map, &kv_full[s], 0, r0, r1, r2, r3, policy);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {  // let in-flight copies land before the CTA can exit
+      for (int k = (i > 2 ? i - 2 : 0); k < i; ++k) mbar_drain(&kv_full[k & 1], (k >> 1) & 1);
+      for (int k = (nq > 2 ? nq - 2 : 0); k < nq; ++k) mbar_drain(&q_full[k & 1], (k >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issuer
+    if (lane == 0 && n > 0) {
+      int sg = -1;
+      int prev_sg = 0;
+      bool prev_start = false;
+      bool ok = true;
+      auto issue_pv = [&](int j, int seg, bool seg_start) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&p_full[s], (j >> 1) & 1, wctx)) return false;
+        if (seg_start && !mbar_wait(&o_empty[seg & 1], ((seg >> 1) & 1) ^ 1, wctx)) return false;
+        tc_fence_after();
+        const uint32_t st = smem_u32(stage_mem + s * kStageBytes);
+        const uint32_t pb = smem_u32(p_mem + s * kPBytes);
+        const uint32_t obuf = tmem_base + kColO + 64u * (seg & 1);
+#pragma unroll
+        for (int mb = 0; mb < 4; ++mb) {
+#pragma unroll
+          for (int kk = 0; kk < kRows / 16; ++kk) {
+            const uint64_t ad = sdesc_sw128(st + (2 * mb) * kChunkBytes + kk * 2048, kChunkBytes, 1024);
+            const uint64_t bd = sdesc_sw128(pb + kk * 32, 16, 1024);
+            umma_bf16(obuf + 16 * mb, ad, bd, kIdescO, (seg_start && kk == 0) ? 0u : 1u);
+          }
+        }
+        umma_commit(&kv_empty[s]);
+        umma_commit(&p_empty[s]);
+        return true;
+      };
+      for (int i = 0; i < n && ok; ++i) {
+        const int64_t u = u0 + i;
+        const int tile = static_cast<int>(u % kTilesPerTok);
+        const bool seg_start = (i == 0 || tile == 0);
+        const bool seg_end = (i == n - 1 || tile == kTilesPerTok - 1);
+        if (seg_start) {
+          ++sg;
+          if (!mbar_wait(&q_full[sg & 1], (sg >> 1) & 1, wctx)) break;
+        }
+        const int s = i & 1;
+        if (!mbar_wait(&kv_full[s], (i >> 1) & 1, wctx)) break;
+        if (!mbar_wait(&s_empty[s], ((i >> 1) & 1) ^ 1, wctx)) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(stage_mem + s * kStageBytes);
+        const uint32_t qb = smem_u32(q_mem + (sg & 1) * kQBytes);
+#pragma unroll 4
+        for (int k = 0; k < kChunks * 4; ++k) {
+          const uint32_t off = (k >> 2) * kChunkBytes + (k & 3) * 32;
+          const uint32_t qoff = (k >> 2) * kQChunkBytes + (k & 3) * 32;
+          umma_bf16(tmem_base + kColS + 16u * s, sdesc_sw128(st + off, 16, 1024),
+                    sdesc_sw128(qb + qoff, 16, 1024), kIdescS, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[s]);
+        if (seg_end) umma_commit(&q_empty[sg & 1]);
+        if (i > 0) ok = issue_pv(i - 1, prev_sg, prev_start);
+        prev_sg = sg;
+        prev_start = seg_start;
+        if (ok && i == n - 1) ok = issue_pv(i, sg, seg_start);
+      }
+      umma_commit(drain);
+      mbar_drain(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------ softmax warps
+    // Every bounded wait is followed, before any branch, by a named barrier
+    // that ANDs the threads' results, so the 128 threads always meet the same
+    // barriers and leave the loop together if a wait gave up.
+    const int sp = warp & 3;
+    const int e = tid - 64;              // 0..127
+    const int h = e >> 3;                // head owned in the reduction phase
+    const int g = e & 7;                 // 8-row group of that head
+    const uint32_t lane_base = static_cast<uint32_t>(sp * 32) << 16;
+    const int srow = 16 * sp + (lane & 15);  // S^T row held by this thread (lane < 16)
+    float m_run = -INFINITY, l_run = 0.f;
+    int sg = -1, seg_first_tile = 0;
+    for (int i = 0; i < n; ++i) {
+      const int64_t u = u0 + i;
+      const int t = static_cast<int>(u / kTilesPerTok);
+      const int tile = static_cast<int>(u % kTilesPerTok);
+      const bool seg_start = (i == 0 || tile == 0);
+      const bool seg_end = (i == n - 1 || tile == kTilesPerTok - 1);
+      if (seg_start) { ++sg; m_run = -INFINITY; l_run = 0.f; seg_first_tile = tile; }
+      const int s = i & 1;
+      const int idx = __ldg(p.indices + static_cast<int64_t>(t) * kTopK + tile * kRows + srow);
+      const bool valid = idx >= 0 && idx < p.num_slots;
+
+      bool ok = mbar_wait(&s_full[s], (i >> 1) & 1, wctx);
+      tc_fence_after();
+      float sv[16];
+      tmem_ld16(tmem_base + lane_base + kColS + 16u * s, sv);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_empty[s]);
+      if (lane < 16) {
+#pragma unroll
+        for (int hh = 0; hh < kHeads; ++hh)
+          sx[hh * kRows + srow] = valid ? sv[hh] * p.scale_log2 : -INFINITY;
+      }
+      if (!named_barrier_and(1, 128, ok)) break;
+
+      float x[8];
+      {
+        const float4 a = *reinterpret_cast<const float4*>(sx + h * kRows + 8 * g);
+        const float4 b = *reinterpret_cast<const float4*>(sx + h * kRows + 8 * g + 4);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+      }
+      float mt = x[0];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) mt = fmaxf(mt, x[k]);
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+      float m_new = m_run, alpha = 1.f;
+      bool need_rescale = false;
+      if (seg_start) {
+        m_new = mt;
+      } else if (mt > m_run + kRescaleThreshold) {
+        m_new = mt;
+        alpha = exp2f(m_run - m_new);  // 0 when m_run == -inf
+        need_rescale = true;
+      }
+      float pr[8], sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        pr[k] = (m_new == -INFINITY) ? 0.f : exp2f(x[k] - m_new);
+        sum += pr[k];
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      l_run = l_run * alpha + sum;
+      m_run = m_new;
+      if (g == 0) {
+        alpha_smem[h] = alpha;
+        if (need_rescale) *rescale_flag = 1;
+      }
+      // P buffer s was last read by the PV of tile i-2.
+      if (i >= 2) ok = mbar_wait(&p_empty[s], ((i - 2) >> 1) & 1, wctx);
+      {
+        __nv_bfloat162 q0 = __floats2bfloat162_rn(pr[0], pr[1]);
+        __nv_bfloat162 q1 = __floats2bfloat162_rn(pr[2], pr[3]);
+        __nv_bfloat162 q2 = __floats2bfloat162_rn(pr[4], pr[5]);
+        __nv_bfloat162 q3 = __floats2bfloat162_rn(pr[6], pr[7]);
+        uint4 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&q0);
+        pk.y = *reinterpret_cast<uint32_t*>(&q1);
+        pk.z = *reinterpret_cast<uint32_t*>(&q2);
+        pk.w = *reinterpret_cast<uint32_t*>(&q3);
+        uint8_t* dst = p_mem + s * kPBytes + (h >> 3) * 1024 + (h & 7) * 128 + ((g ^ (h & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = pk;
+      }
+      if (!named_barrier_and(1, 128, ok)) break;
+      if (*rescale_flag) {
+        // O must hold PV(i-1) before it is rescaled (same segment: i >= 1).
+        ok = mbar_wait(&p_empty[(i - 1) & 1], ((i - 1) >> 1) & 1, wctx);
+        tc_fence_after();
+        const uint32_t obuf = tmem_base + lane_base + kColO + 64u * (sg & 1);
+#pragma unroll
+        for (int mb = 0; mb < 4; ++mb) {
+          float o[16];
+          tmem_ld16(obuf + 16 * mb, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int hh = 0; hh < kHeads; ++hh) o[hh] *= alpha_smem[hh];
+          tmem_st16(obuf + 16 * mb, o);
+        }
+        tmem_wait_st();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      if (!named_barrier_and(1, 128, ok)) break;
+      if (e == 0) {
+        *rescale_flag = 0;
+        mbar_arrive(&p_full[s]);
+      }
+
+      if (seg_end) {
+        // ---- finalise the segment: wait for its last PV, drain O.
+        ok = mbar_wait(&p_empty[s], (i >> 1) & 1, wctx);
+        tc_fence_after();
+        if (g == 0) { ml_smem[2 * h] = m_run; ml_smem[2 * h + 1] = l_run; }
+        float o[4][16];
+        const uint32_t obuf = tmem_base + lane_base + kColO + 64u * (sg & 1);
+#pragma unroll
+        for (int mb = 0; mb < 4; ++mb) tmem_ld16(obuf + 16 * mb, o[mb]);
+        tmem_wait_ld();
+        tc_fence_before();
+        if (!named_barrier_and(1, 128, ok)) break;
+        if (e == 0) mbar_arrive(&o_empty[sg & 1]);
+        const int col = 32 * sp + lane;
+        const bool whole = (seg_first_tile == 0 && tile == kTilesPerTok - 1);
+        if (whole) {
+          __nv_bfloat16* out = p.out + static_cast<int64_t>(t) * kHeads * kCkv;
+#pragma unroll
+          for (int hh = 0; hh < kHeads; ++hh) {
+            const float l = ml_smem[2 * hh + 1];
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+            for (int mb = 0; mb < 4; ++mb)
+              out[hh * kCkv + 128 * mb + col] = __float2bfloat16_rn(o[mb][hh] * inv);
+          }
+          if (e < kHeads) {
+            const float l = ml_smem[2 * e + 1];
+            p.lse[static_cast<int64_t>(t) * kHeads + e] =
+                l > 0.f ? ml_smem[2 * e] + log2f(l) : -INFINITY;
+          }
+        } else {
+          const int64_t rec = static_cast<int64_t>(blockIdx.x) * p.kmax + (t - t_first);
+          float* po = p.part_o + rec * kHeads * kCkv;
+#pragma unroll
+          for (int hh = 0; hh < kHeads; ++hh)
+#pragma unroll
+            for (int mb = 0; mb < 4; ++mb) po[hh * kCkv + 128 * mb + col] = o[mb][hh];
+          if (e < kHeads) {
+            p.part_ml[rec * 2 * kHeads + 2 * e] = ml_smem[2 * e];
+            p.part_ml[rec * 2 * kHeads + 2 * e + 1] = ml_smem[2 * e + 1];
+          }
+        }
+        named_barrier_sync(1, 128);  // ml_smem is rewritten by the next segment
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// One CTA per token; does nothing for tokens a single CTA finished.
+__global__ void __launch_bounds__(256) attention_combine_kernel(const Params p, int grid) {
+  const int t = blockIdx.x;
+  const int64_t total = static_cast<int64_t>(p.num_tokens) * kTilesPerTok;
+  const int64_t a = static_cast<int64_t>(t) * kTilesPerTok, z = a + kTilesPerTok;
+  int c = static_cast<int>(a * grid / total);
+  while (c > 0 && unit_start(total, c, grid) > a) --c;
+  while (unit_start(total, c + 1, grid) <= a) ++c;
+  if (unit_start(total, c, grid) <= a && unit_start(total, c + 1, grid) >= z) return;
+
+  const int tid = threadIdx.x;
+  const int h = tid >> 4;            // 16 threads per head
+  const int c0 = (tid & 15) * 32;    // 32 columns each
+  float M = -INFINITY;
+  for (int cc = c; cc < grid && unit_start(total, cc, grid) < z; ++cc) {
+    const int64_t rec = static_cast<int64_t>(cc) * p.kmax +
+                        (t - static_cast<int>(unit_start(total, cc, grid) / kTilesPerTok));
+    M = fmaxf(M, p.part_ml[rec * 2 * kHeads + 2 * h]);
+  }
+  float l = 0.f;
+  float acc[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) acc[k] = 0.f;
+  if (M != -INFINITY) {
+    for (int cc = c; cc < grid && unit_start(total, cc, grid) < z; ++cc) {
+      const int64_t rec = static_cast<int64_t>(cc) * p.kmax +
+                          (t - static_cast<int>(unit_start(total, cc, grid) / kTilesPerTok));
+      const float mi = p.part_ml[rec * 2 * kHeads + 2 * h];
+      const float li = p.part_ml[rec * 2 * kHeads + 2 * h + 1];
+      if (mi == -INFINITY) continue;
+      const float wgt = exp2f(mi - M);
+      l += li * wgt;
+      const float4* src = reinterpret_cast<const float4*>(p.part_o + (rec * kHeads + h) * kCkv + c0);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float4 v = src[k];
+        acc[4 * k] += v.x * wgt; acc[4 * k + 1] += v.y * wgt;
+        acc[4 * k + 2] += v.z * wgt; acc[4 * k + 3] += v.w * wgt;
+      }
+    }
+  }
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  __nv_bfloat16* out = p.out + (static_cast<int64_t>(t) * kHeads + h) * kCkv + c0;
+#pragma unroll
+  for (int k = 0; k < 32; k += 2)
+    *reinterpret_cast<__nv_bfloat162*>(out + k) = __floats2bfloat162_rn(acc[k] * inv, acc[k + 1] * inv);
+  if ((tid & 15) == 0)
+    p.lse[static_cast<int64_t>(t) * kHeads + h] = l > 0.f ? M + log2f(l) : -INFINITY;
+}
+
+inline int grid_for(int num_tokens, int num_sms) {
+  const int64_t units = static_cast<int64_t>(num_tokens) * kTilesPerTok;
+  return static_cast<int>(units < num_sms ? units : num_sms);
+}
+
+inline int kmax_for(int num_tokens, int grid) {
+  const int64_t units = static_cast<int64_t>(num_tokens) * kTilesPerTok;
+  const int64_t per = (units + grid - 1) / grid;
+  return static_cast<int>((per + kTilesPerTok - 1) / kTilesPerTok + 1);
+}
+
+inline size_t workspace_for(int num_tokens, int num_sms) {
+  if (num_tokens <= 0) return kWorkspaceHeader;
+  const int grid = grid_for(num_tokens, num_sms);
+  const size_t recs = static_cast<size_t>(grid) * kmax_for(num_tokens, grid);
+  return kWorkspaceHeader + recs * kHeads * (kCkv + 2) * sizeof(float);
+}
+
+std::once_flag g_attr_once[64];
+int g_attr_status[64];
+
+}  // namespace attn
+}  // namespace dsa
+
+using namespace dsa;
+
+extern "C" size_t dsa_attention_workspace_bytes(int32_t num_tokens) {
+  DeviceInfo info;
+  // Without a usable device, size for the largest SM count of the family.
+  const int sms = current_device_info(&info) == DSA_OK ? info.num_sms : 160;
+  return attn::workspace_for(num_tokens, sms);
+}
+
+extern "C" int dsa_attention_run(const void* q_nope, const void* q_pe, const void* ckv_cache,
+                                 const void* kpe_cache, int64_t num_slots,
+                                 const int32_t* sparse_indices, int32_t num_tokens,
+                                 float sm_scale, void* output, float* lse, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (num_tokens < 0 || num_tokens > attn::kMaxTokens) return DSA_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return DSA_OK;
+  if (!q_nope || !q_pe || !ckv_cache || !kpe_cache || !sparse_indices || !output || !lse ||
+      !workspace)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (num_slots < 1 || num_slots > 0x7FFFFFFF) return DSA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q_nope) || !aligned16(q_pe) || !aligned16(ckv_cache) || !aligned16(kpe_cache) ||
+      !aligned16(output) || !aligned16(workspace))
+    return DSA_ERR_MISALIGNED;
+  if ((reinterpret_cast<uintptr_t>(sparse_indices) | reinterpret_cast<uintptr_t>(lse)) & 3u)
+    return DSA_ERR_MISALIGNED;
+
+  DeviceInfo info;
+  int st = current_device_info(&info);
+  if (st != DSA_OK) return st;
+  if (static_cast<size_t>(attn::kSmemBytes) > info.max_smem_optin) return DSA_ERR_UNSUPPORTED_DEVICE;
+  if (workspace_bytes < attn::workspace_for(num_tokens, info.num_sms))
+    return DSA_ERR_WORKSPACE_TOO_SMALL;
+  std::call_once(attn::g_attr_once[info.device], [&]() {
+    attn::g_attr_status[info.device] =
+        cudaFuncSetAttribute(attn::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             attn::kSmemBytes) == cudaSuccess
+            ? DSA_OK
+            : DSA_ERR_CUDA;
+  });
+  if (attn::g_attr_status[info.device] != DSA_OK) return attn::g_attr_status[info.device];
+
+  CUtensorMap ckv_map, kpe_map, qn_map, qp_map;
+  const uint64_t rows_q = static_cast<uint64_t>(num_tokens) * attn::kHeads;
+  if ((st = encode_tmap_2d(&ckv_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, ckv_cache, attn::kCkv,
+                           static_cast<uint64_t>(num_slots), attn::kCkv * 2, 64, 1)) != DSA_OK)
+    return st;
+  if ((st = encode_tmap_2d(&kpe_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kpe_cache, attn::kKpe,
+                           static_cast<uint64_t>(num_slots), attn::kKpe * 2, 64, 1)) != DSA_OK)
+    return st;
+  if ((st = encode_tmap_2d(&qn_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q_nope, attn::kCkv, rows_q,
+                           attn::kCkv * 2, 64, attn::kHeads)) != DSA_OK)
+    return st;
+  if ((st = encode_tmap_2d(&qp_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q_pe, attn::kKpe, rows_q,
+                           attn::kKpe * 2, 64, attn::kHeads)) != DSA_OK)
+    return st;
+
+  const int grid = attn::grid_for(num_tokens, info.num_sms);
+  const int kmax = attn::kmax_for(num_tokens, grid);
+  const size_t recs = static_cast<size_t>(grid) * kmax;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  attn::Params prm;
+  prm.indices = sparse_indices;
+  prm.out = static_cast<__nv_bfloat16*>(output);
+  prm.lse = lse;
+  prm.part_o = reinterpret_cast<float*>(ws + kWorkspaceHeader);
+  prm.part_ml = prm.part_o + recs * attn::kHeads * attn::kCkv;
+  prm.status = reinterpret_cast<unsigned int*>(ws);
+  prm.num_slots = num_slots;
+  prm.num_tokens = num_tokens;
+  prm.kmax = kmax;
+  prm.scale_log2 = sm_scale * 1.4426950408889634f;
+
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  attn::attention_kernel<<<grid, attn::kThreads, attn::kSmemBytes, s>>>(ckv_map, kpe_map, qn_map,
+                                                                       qp_map, prm);
+  attn::attention_combine_kernel<<<num_tokens, 256, 0, s>>>(prm, grid);
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  return DSA_OK;
+}

@@ -1,0 +1,590 @@
+// indexer.cu -- DSA lightning indexer (decode) for sm_100a.
+//
+// Replaces dsa_topk_run_ms / run() of dsa_indexer/solution/triton/kernel.py.
+// Two kernels, both launched on the caller's stream with no host sync:
+//
+// 1. indexer_score_kernel (persistent, one CTA per SM).  The work list is the
+//    concatenation over requests of 128-token tiles (two 64-token pages);
+//    CTA c takes the contiguous slice [c*U/G, (c+1)*U/G) of the U tiles, so
+//    load balance does not depend on how seq_lens are distributed.  Roles:
+//      warp 0      TMA producer: raw FP8 pages (64 rows x 128 B, 128-byte
+//                  swizzle) straight from the paged cache into an 8-deep
+//                  shared-memory ring, and q[b] (64 heads x 128 B) when the
+//                  request changes.  Nothing is dequantised in HBM
+//                  (the reference writes an fp32 copy of K, kernel.py:108-135).
+//      warp 1      MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 tokens,
+//                  N = 64 heads, K = 128 (4 x K32), fp32 accumulator in TMEM,
+//                  4 accumulator stages.
+//      warps 2-5   epilogue: each thread owns one token row of the TMEM
+//                  accumulator (64 head columns) and computes
+//                  sum_h w_h * relu(scale_tok * acc_h) in registers -- no
+//                  cross-thread reduction -- then stores one fp32 score.
+//    Scores go to a [batch, max_pages*64] fp32 workspace (L2-resident at
+//    decode sizes); per-head scores never exist in memory (the reference
+//    materialises [64, L] fp32, kernel.py:293-300).
+//
+// 2. topk_select_kernel (one CTA per request).  Exact top-min(L, 2048) by
+//    radix select on the 64-bit key (order(score) << 32 | ~token), which
+//    encodes "score descending, then lower token index first" as one total
+//    order.  Pass 1 histograms the top 11 key bits over all L scores; pass 2
+//    moves the winners of higher bins to the output and the boundary bin to
+//    a shared-memory candidate list, which later passes refine.  The 2048
+//    winners are bitonic-sorted and translated to global slot ids through
+//    the block table (kernel.py:156-169), then -1 padded (kernel.py:206).
+#include <mutex>
+
+#include "host.h"
+#include "ptx.cuh"
+
+namespace dsa {
+namespace ix {
+
+constexpr int kPage = DSA_PAGE_SIZE;                      // 64 tokens per page
+constexpr int kHeads = DSA_INDEX_HEADS;                   // 64
+constexpr int kDim = DSA_INDEX_DIM;                       // 128 fp8 per token
+constexpr int kPageBytes = DSA_INDEX_PAGE_BYTES;          // 8448
+constexpr int kPageRows = kPageBytes / 128;               // page = 66 rows of 128 B
+constexpr int kPageDataBytes = kPage * kDim;              // 8192
+constexpr int kTileTok = 2 * kPage;                       // 128 tokens per tile
+constexpr int kStageBytes = 2 * kPageDataBytes;           // 16384
+constexpr int kStages = 8;
+constexpr int kAccStages = 4;
+constexpr int kTmemCols = kAccStages * kHeads;            // 256
+constexpr int kThreads = 192;
+constexpr int kMaxBatch = 8192;
+constexpr int kMaxPagesPerSeq = 1 << 20;
+constexpr int64_t kMaxPool = (int64_t(1) << 31) / kPageRows - 1;
+
+// e4m3 x e4m3 -> f32, A (tokens) and B (heads) K-major, M = 128, N = 64.
+constexpr uint32_t kIdesc = idesc_make(0, 0, false, false, 128, 64);
+
+constexpr int kOffStage = 0;
+constexpr int kOffQ = kOffStage + kStages * kStageBytes;          // 131072
+constexpr int kOffBar = kOffQ + 2 * kPageDataBytes;               // 147456
+constexpr int kNumBars = 2 * kStages + 4 + 2 * kAccStages + 1;
+constexpr int kOffMisc = kOffBar + 256;
+constexpr int kOffTiles = kOffMisc + 64;
+static_assert(kNumBars * 8 <= 256, "barrier area");
+
+inline size_t score_smem_bytes(int batch) {
+  return 1024 + kOffTiles + sizeof(int) * static_cast<size_t>(batch + 1);
+}
+
+struct ScoreParams {
+  const uint8_t* k_cache;
+  const float* weights;
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  float* scores;
+  unsigned int* status;
+  int64_t num_pages;
+  int batch;
+  int max_pages;
+  int score_stride;  // = max_pages * 64
+};
+
+__device__ __forceinline__ int clamp_len(int L, int max_len, unsigned int* status) {
+  if (L < 0 || L > max_len) {
+    atomicOr(status, DSA_DEV_BAD_SEQ_LEN);
+    L = L < 0 ? 0 : max_len;
+  }
+  return L;
+}
+
+__device__ __forceinline__ int page_id(const ScoreParams& p, int b, int page_idx) {
+  int pid = __ldg(p.block_table + static_cast<int64_t>(b) * p.max_pages + page_idx);
+  if (pid < 0 || pid >= p.num_pages) {
+    atomicOr(p.status, DSA_DEV_BAD_PAGE);
+    pid = 0;
+  }
+  return pid;
+}
+
+// Walks the CTA's slice of the tile list: (request b, tile j within b).
+struct TileWalk {
+  const int* tile_off;
+  int batch;
+  int b;
+  int j;
+  __device__ void start(int64_t u) {
+    int lo = 0, hi = batch;  // find b with tile_off[b] <= u < tile_off[b+1]
+    while (lo < hi) {
+      int mid = (lo + hi) >> 1;
+      if (tile_off[mid + 1] <= u) lo = mid + 1; else hi = mid;
+    }
+    b = lo;
+    j = static_cast<int>(u - tile_off[b]);
+  }
+  __device__ void next() {
+    ++j;
+    while (b < batch && j >= tile_off[b + 1] - tile_off[b]) { ++b; j = 0; }
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap qmap, const ScoreParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stage_mem = smem + kOffStage;
+  uint8_t* q_mem = smem + kOffQ;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* qfull = bars + 2 * kStages;
+  uint64_t* qempty = qfull + 2;
+  uint64_t* accfull = qempty + 2;
+  uint64_t* accempty = accfull + kAccStages;
+  uint64_t* drain = accempty + kAccStages;
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  int* abort_flag = reinterpret_cast<int*>(smem + kOffMisc + 4);
+  int* warp_sums = reinterpret_cast<int*>(smem + kOffMisc + 16);  // 6 ints
+  int* tile_off = reinterpret_cast<int*>(smem + kOffTiles);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int max_len = p.max_pages * kPage;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&qfull[s], 1); mbar_init(&qempty[s], 1); }
+    for (int s = 0; s < kAccStages; ++s) { mbar_init(&accfull[s], 1); mbar_init(&accempty[s], 128); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { prefetch_tensor_map(&kmap); prefetch_tensor_map(&qmap); }
+  if (warp == 1) tmem_alloc(tmem_base_smem, kTmemCols);
+
+  // Tile prefix sums over requests (each CTA recomputes them: seq_lens stay
+  // on the device and B is small).
+  {
+    const int chunk = (p.batch + kThreads - 1) / kThreads;
+    const int lo = min(p.batch, tid * chunk), hi = min(p.batch, lo + chunk);
+    int local = 0;
+    for (int b = lo; b < hi; ++b) {
+      int L = clamp_len(__ldg(p.seq_lens + b), max_len, p.status);
+      local += (L + kTileTok - 1) / kTileTok;
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    int base = 0;
+    for (int w = 0; w < warp; ++w) base += warp_sums[w];
+    int run = base + incl - local;
+    for (int b = lo; b < hi; ++b) {
+      tile_off[b] = run;
+      int L = clamp_len(__ldg(p.seq_lens + b), max_len, p.status);
+      run += (L + kTileTok - 1) / kTileTok;
+    }
+    if (tid == kThreads - 1) tile_off[p.batch] = base + incl;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem_base = *tmem_base_smem;
+  const int64_t total = tile_off[p.batch];
+  const int64_t u0 = total * blockIdx.x / gridDim.x;
+  const int64_t u1 = total * (blockIdx.x + 1) / gridDim.x;
+  const WaitCtx wctx{abort_flag, p.status};
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0 && u0 < u1) {
+      const uint64_t policy = make_policy_evict_first();
+      TileWalk w{tile_off, p.batch, 0, 0};
+      w.start(u0);
+      int cur_b = -1, nq = 0;
+      int64_t n = 0;
+      for (int64_t u = u0; u < u1; ++u, ++n, w.next()) {
+        if (w.b != cur_b) {
+          cur_b = w.b;
+          const int slot = nq & 1;
+          if (!mbar_wait(&qempty[slot], ((nq >> 1) & 1) ^ 1, wctx)) break;
+          mbar_arrive_expect_tx(&qfull[slot], kPageDataBytes);
+          tma_load_2d(q_mem + slot * kPageDataBytes, &qmap, &qfull[slot], 0, cur_b * kHeads);
+          ++nq;
+        }
+        const int s = static_cast<int>(n % kStages);
+        const uint32_t ph = static_cast<uint32_t>((n / kStages) & 1);
+        if (!mbar_wait(&empty[s], ph ^ 1, wctx)) break;
+        const int L = clamp_len(__ldg(p.seq_lens + cur_b), max_len, p.status);
+        const int req_pages = (L + kPage - 1) / kPage;
+        const int npg = (2 * w.j + 1 < req_pages) ? 2 : 1;
+        mbar_arrive_expect_tx(&full[s], npg * kPageDataBytes);
+        for (int g = 0; g < npg; ++g) {
+          const int pid = page_id(p, cur_b, 2 * w.j + g);
+          tma_load_2d_hint(stage_mem + s * kStageBytes + g * kPageDataBytes, &kmap, &full[s], 0,
+                           pid * kPageRows, policy);
+        }
+      }
+      // Let every copy this thread issued land before the CTA can exit.
+      const int64_t issued = n;
+      for (int64_t k = (issued > kStages ? issued - kStages : 0); k < issued; ++k)
+        mbar_drain(&full[k % kStages], static_cast<uint32_t>((k / kStages) & 1));
+      for (int k = (nq > 2 ? nq - 2 : 0); k < nq; ++k) mbar_drain(&qfull[k & 1], (k >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issuer
+    if (lane == 0 && u0 < u1) {
+      TileWalk w{tile_off, p.batch, 0, 0};
+      w.start(u0);
+      int cur_b = -1, nq = 0, slot = 0;
+      int64_t n = 0;
+      for (int64_t u = u0; u < u1; ++u, ++n, w.next()) {
+        if (w.b != cur_b) {
+          cur_b = w.b;
+          if (nq > 0) umma_commit(&qempty[(nq - 1) & 1]);
+          slot = nq & 1;
+          if (!mbar_wait(&qfull[slot], (nq >> 1) & 1, wctx)) break;
+          ++nq;
+        }
+        const int s = static_cast<int>(n % kStages);
+        const uint32_t ph = static_cast<uint32_t>((n / kStages) & 1);
+        const int a = static_cast<int>(n % kAccStages);
+        const uint32_t aph = static_cast<uint32_t>((n / kAccStages) & 1);
+        if (!mbar_wait(&full[s], ph, wctx)) break;
+        if (!mbar_wait(&accempty[a], aph ^ 1, wctx)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(stage_mem + s * kStageBytes);
+        const uint32_t b_addr = smem_u32(q_mem + slot * kPageDataBytes);
+#pragma unroll
+        for (int k = 0; k < kDim / 32; ++k) {
+          umma_f8(tmem_base + a * kHeads, sdesc_sw128(a_addr + 32 * k, 16, 1024),
+                  sdesc_sw128(b_addr + 32 * k, 16, 1024), kIdesc, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+        umma_commit(&accfull[a]);
+      }
+      umma_commit(drain);
+      mbar_drain(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------ epilogue
+    const int sp = warp & 3;          // TMEM sub-partition this warp may access
+    const int row = sp * 32 + lane;   // token row of the 128-token tile
+    if (u0 < u1) {
+      TileWalk w{tile_off, p.batch, 0, 0};
+      w.start(u0);
+      int cur_b = -1, L = 0;
+      float wt[kHeads];
+      int64_t n = 0;
+      for (int64_t u = u0; u < u1; ++u, ++n, w.next()) {
+        if (w.b != cur_b) {
+          cur_b = w.b;
+          L = clamp_len(__ldg(p.seq_lens + cur_b), max_len, p.status);
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) wt[h] = __ldg(p.weights + cur_b * kHeads + h);
+        }
+        const int tok = w.j * kTileTok + row;
+        const bool valid = tok < L;
+        float scale = 0.f;
+        if (valid) {
+          const int pid = page_id(p, cur_b, tok >> 6);
+          scale = __ldg(reinterpret_cast<const float*>(
+              p.k_cache + static_cast<int64_t>(pid) * kPageBytes + kPageDataBytes + (tok & 63) * 4));
+        }
+        const int a = static_cast<int>(n % kAccStages);
+        const uint32_t aph = static_cast<uint32_t>((n / kAccStages) & 1);
+        if (!mbar_wait(&accfull[a], aph, wctx)) break;
+        tc_fence_after();
+        float acc[kHeads];
+        {
+          float lo[32], hi[32];
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + a * kHeads;
+          tmem_ld32(taddr, lo);
+          tmem_ld32(taddr + 32, hi);
+          tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < 32; ++h) { acc[h] = lo[h]; acc[h + 32] = hi[h]; }
+        }
+        tc_fence_before();
+        mbar_arrive(&accempty[a]);
+        if (valid) {
+          // relu(v) written as the reference does: v <= 0 ? 0 : v (NaN passes).
+          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+          for (int h = 0; h < kHeads; h += 4) {
+            float x0 = acc[h] * scale, x1 = acc[h + 1] * scale;
+            float x2 = acc[h + 2] * scale, x3 = acc[h + 3] * scale;
+            s0 += (x0 <= 0.f ? 0.f : x0) * wt[h];
+            s1 += (x1 <= 0.f ? 0.f : x1) * wt[h + 1];
+            s2 += (x2 <= 0.f ? 0.f : x2) * wt[h + 2];
+            s3 += (x3 <= 0.f ? 0.f : x3) * wt[h + 3];
+          }
+          p.scores[static_cast<int64_t>(cur_b) * p.score_stride + tok] = (s0 + s1) + (s2 + s3);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------ top-k select
+constexpr int kSelThreads = 1024;
+constexpr int kTopK = DSA_TOPK;
+constexpr int kBins = 2048;
+constexpr int kCandCap = 16384;
+constexpr size_t kSelSmem = sizeof(uint64_t) * (kTopK + kCandCap) + sizeof(uint32_t) * kBins + 256;
+
+struct SelectParams {
+  const float* scores;
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  int32_t* out;
+  int score_stride;
+  int max_pages;
+};
+
+__device__ __forceinline__ uint64_t composite(float s, int tok) {
+  return (static_cast<uint64_t>(score_key(s)) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(tok));
+}
+
+// Inclusive prefix sum over the 1024 threads of the block.
+__device__ __forceinline__ int block_scan_incl(int v, int* warp_tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  if (lane == 31) warp_tot[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int t = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int u = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += u;
+    }
+    warp_tot[lane] = t;  // inclusive totals
+  }
+  __syncthreads();
+  const int add = warp > 0 ? warp_tot[warp - 1] : 0;
+  __syncthreads();
+  return v + add;
+}
+
+// Finds the bin d (scanning from the highest bin down) that holds the
+// need-th largest element; returns d, the count strictly above d and hist[d].
+__device__ __forceinline__ void find_bin(const uint32_t* hist, int need, int* warp_tot, int* res) {
+  const int t = threadIdx.x;
+  const int hi = kBins - 1 - 2 * t, lo = hi - 1;
+  const int a = static_cast<int>(hist[hi]), c = static_cast<int>(hist[lo]);
+  const int incl = block_scan_incl(a + c, warp_tot);
+  const int excl = incl - a - c;
+  if (excl < need && need <= excl + a) { res[0] = hi; res[1] = excl; res[2] = a; }
+  else if (excl + a < need && need <= incl) { res[0] = lo; res[1] = excl + a; res[2] = c; }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const SelectParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint64_t* sel = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* cand = sel + kTopK;
+  uint32_t* hist = reinterpret_cast<uint32_t*>(cand + kCandCap);
+  int* warp_tot = reinterpret_cast<int*>(hist + kBins);  // 32 ints
+  int* res = warp_tot + 32;                               // bin, above, count
+  int* counters = res + 4;                                // nsel, ncand
+
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int max_len = p.max_pages * kPage;
+  int L = __ldg(p.seq_lens + b);
+  L = L < 0 ? 0 : (L > max_len ? max_len : L);  // the score kernel flags bad lengths
+  const float* row = p.scores + static_cast<int64_t>(b) * p.score_stride;
+  const int K = L < kTopK ? L : kTopK;
+
+  if (L <= kTopK) {
+    for (int i = tid; i < kTopK; i += kSelThreads) sel[i] = i < L ? composite(row[i], i) : 0ull;
+    __syncthreads();
+  } else {
+    // Pass 1: histogram of the top 11 key bits over all L scores.
+    for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
+    if (tid == 0) { counters[0] = 0; counters[1] = 0; }
+    __syncthreads();
+    for (int i = tid; i < L; i += kSelThreads) atomicAdd(&hist[score_key(row[i]) >> 21], 1u);
+    __syncthreads();
+    find_bin(hist, K, warp_tot, res);
+    const uint32_t bin1 = static_cast<uint32_t>(res[0]);
+    int need = K - res[1];
+    int count = res[2];
+    // Pass 2: higher bins are winners; the boundary bin becomes candidates.
+    for (int i = tid; i < L; i += kSelThreads) {
+      const float s = row[i];
+      const uint32_t d = score_key(s) >> 21;
+      if (d > bin1) {
+        sel[atomicAdd(&counters[0], 1)] = composite(s, i);
+      } else if (d == bin1) {
+        const int c = atomicAdd(&counters[1], 1);
+        if (c < kCandCap) cand[c] = composite(s, i);
+      }
+    }
+    __syncthreads();
+    const int ncand = counters[1];
+    const bool in_smem = ncand <= kCandCap;
+    uint64_t prefix = static_cast<uint64_t>(bin1) << 53;
+    uint64_t mask = static_cast<uint64_t>(0x7FF) << 53;
+    // Refine the boundary: 11-bit digits of the remaining 53 key bits.
+    const int shifts[5] = {42, 31, 20, 9, 0};
+    const int widths[5] = {11, 11, 11, 11, 9};
+    for (int pass = 0; pass < 5 && count != need; ++pass) {
+      const int sh = shifts[pass];
+      const uint64_t dm = (static_cast<uint64_t>(1) << widths[pass]) - 1;
+      for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
+      __syncthreads();
+      if (in_smem) {
+        for (int i = tid; i < ncand; i += kSelThreads) {
+          const uint64_t c = cand[i];
+          if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
+        }
+      } else {
+        for (int i = tid; i < L; i += kSelThreads) {
+          const uint64_t c = composite(row[i], i);
+          if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
+        }
+      }
+      __syncthreads();
+      find_bin(hist, need, warp_tot, res);
+      prefix |= static_cast<uint64_t>(res[0]) << sh;
+      mask |= dm << sh;
+      need -= res[1];
+      count = res[2];
+    }
+    // Collect the boundary-bin winners: (c & mask) >= prefix.
+    if (in_smem) {
+      for (int i = tid; i < ncand; i += kSelThreads) {
+        const uint64_t c = cand[i];
+        if ((c & mask) >= prefix) sel[atomicAdd(&counters[0], 1)] = c;
+      }
+    } else {
+      for (int i = tid; i < L; i += kSelThreads) {
+        const uint64_t c = composite(row[i], i);
+        if ((c >> 53) == bin1 && (c & mask) >= prefix) sel[atomicAdd(&counters[0], 1)] = c;
+      }
+    }
+    __syncthreads();
+  }
+
+  // Bitonic sort of the 2048 composite keys, descending.
+  for (int k = 2; k <= kTopK; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const int lo = 2 * j * (tid / j) + (tid % j);
+      const int hi = lo + j;
+      const uint64_t x = sel[lo], y = sel[hi];
+      const bool desc = (lo & k) == 0;
+      if (desc ? (x < y) : (x > y)) { sel[lo] = y; sel[hi] = x; }
+      __syncthreads();
+    }
+  }
+
+  int32_t* out = p.out + static_cast<int64_t>(b) * kTopK;
+  const int32_t* bt = p.block_table + static_cast<int64_t>(b) * p.max_pages;
+  for (int i = tid; i < kTopK; i += kSelThreads) {
+    int32_t v = -1;
+    if (i < K) {
+      const int tok = static_cast<int>(~static_cast<uint32_t>(sel[i]));
+      v = __ldg(bt + (tok >> 6)) * kPage + (tok & 63);
+    }
+    out[i] = v;
+  }
+}
+
+std::once_flag g_attr_once[64];
+int g_attr_status[64];
+
+}  // namespace ix
+}  // namespace dsa
+
+using namespace dsa;
+
+extern "C" size_t dsa_indexer_workspace_bytes(int32_t batch, int32_t max_pages) {
+  if (batch < 0 || max_pages < 0) return 0;
+  return kWorkspaceHeader +
+         sizeof(float) * static_cast<size_t>(batch) * static_cast<size_t>(max_pages) * ix::kPage;
+}
+
+extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cache_fp8,
+                               int64_t num_pages, const float* weights, const int32_t* seq_lens,
+                               const int32_t* block_table, int32_t batch, int32_t max_pages,
+                               int32_t* topk_indices, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  if (batch < 0 || batch > ix::kMaxBatch) return DSA_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return DSA_OK;
+  if (!q_index_fp8 || !k_index_cache_fp8 || !weights || !seq_lens || !block_table ||
+      !topk_indices || !workspace)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (max_pages < 1 || max_pages > ix::kMaxPagesPerSeq) return DSA_ERR_INVALID_ARGUMENT;
+  if (num_pages < 1 || num_pages > ix::kMaxPool) return DSA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q_index_fp8) || !aligned16(k_index_cache_fp8) || !aligned16(workspace))
+    return DSA_ERR_MISALIGNED;
+  if ((reinterpret_cast<uintptr_t>(weights) | reinterpret_cast<uintptr_t>(seq_lens) |
+       reinterpret_cast<uintptr_t>(block_table) | reinterpret_cast<uintptr_t>(topk_indices)) & 3u)
+    return DSA_ERR_MISALIGNED;
+  if (workspace_bytes < dsa_indexer_workspace_bytes(batch, max_pages))
+    return DSA_ERR_WORKSPACE_TOO_SMALL;
+
+  DeviceInfo info;
+  int st = current_device_info(&info);
+  if (st != DSA_OK) return st;
+  const size_t smem1 = ix::score_smem_bytes(batch);
+  if (smem1 > info.max_smem_optin || ix::kSelSmem > info.max_smem_optin)
+    return DSA_ERR_UNSUPPORTED_DEVICE;
+  std::call_once(ix::g_attr_once[info.device], [&]() {
+    bool ok = cudaFuncSetAttribute(ix::indexer_score_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(info.max_smem_optin)) == cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(ix::topk_select_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(ix::kSelSmem)) == cudaSuccess;
+    ix::g_attr_status[info.device] = ok ? DSA_OK : DSA_ERR_CUDA;
+  });
+  if (ix::g_attr_status[info.device] != DSA_OK) return ix::g_attr_status[info.device];
+
+  CUtensorMap kmap, qmap;
+  st = encode_tmap_2d(&kmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_index_cache_fp8, 128,
+                      static_cast<uint64_t>(num_pages) * ix::kPageRows, 128, 128, 64);
+  if (st != DSA_OK) return st;
+  st = encode_tmap_2d(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, q_index_fp8, 128,
+                      static_cast<uint64_t>(batch) * ix::kHeads, 128, 128, 64);
+  if (st != DSA_OK) return st;
+
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  ix::ScoreParams sp;
+  sp.k_cache = static_cast<const uint8_t*>(k_index_cache_fp8);
+  sp.weights = weights;
+  sp.seq_lens = seq_lens;
+  sp.block_table = block_table;
+  sp.scores = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeader);
+  sp.status = static_cast<unsigned int*>(workspace);
+  sp.num_pages = num_pages;
+  sp.batch = batch;
+  sp.max_pages = max_pages;
+  sp.score_stride = max_pages * ix::kPage;
+  ix::indexer_score_kernel<<<info.num_sms, ix::kThreads, smem1, s>>>(kmap, qmap, sp);
+
+  ix::SelectParams selp;
+  selp.scores = sp.scores;
+  selp.seq_lens = seq_lens;
+  selp.block_table = block_table;
+  selp.out = topk_indices;
+  selp.score_stride = sp.score_stride;
+  selp.max_pages = max_pages;
+  ix::topk_select_kernel<<<batch, ix::kSelThreads, ix::kSelSmem, s>>>(selp);
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  return DSA_OK;
+}

@@ -1,0 +1,125 @@
+"""DSA top-k indexer operator (destination-passing style).
+
+``run`` keeps the reference entry point's signature, argument meaning and
+in-place output (dsa_indexer/solution/triton/kernel.py:364-436):
+
+    run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table,
+        topk_indices) -> None
+
+Differences that are deliberate:
+
+* ``seq_lens`` is never copied to the host (the reference calls
+  ``seq_lens.cpu()`` every call, kernel.py:375, which blocks and keys a graph
+  cache on the values); every launch here is asynchronous on the current
+  stream and can be captured into a caller's CUDA graph.
+* The order of equal scores is defined: lower token index first.
+* Bad page ids / lengths do not read out of bounds; they set a sticky status
+  bit (``device_status``) -- with ``DSA_B200_CHECK=1`` each call synchronises
+  and raises on such bits.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _native, workspace
+
+PAGE_SIZE = 64
+NUM_HEADS = 64
+HEAD_DIM = 128
+TOPK = 2048
+PAGE_BYTES = PAGE_SIZE * HEAD_DIM + PAGE_SIZE * 4  # 8448
+
+_CHECK = os.environ.get("DSA_B200_CHECK", "0") not in ("", "0")
+
+
+def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(f"dsa_indexer.run: {msg}")
+
+
+def num_pages_of(k_index_cache_fp8: torch.Tensor) -> int:
+    nbytes = k_index_cache_fp8.numel() * k_index_cache_fp8.element_size()
+    _require(k_index_cache_fp8.element_size() == 1,
+             f"k_index_cache_fp8 must have a 1-byte dtype, got {k_index_cache_fp8.dtype}")
+    _require(nbytes % PAGE_BYTES == 0 and nbytes > 0,
+             f"k_index_cache_fp8 holds {nbytes} bytes, not a positive multiple of {PAGE_BYTES}")
+    return nbytes // PAGE_BYTES
+
+
+@torch.no_grad()
+def run(q_index_fp8: torch.Tensor, k_index_cache_fp8: torch.Tensor, weights: torch.Tensor,
+        seq_lens: torch.Tensor, block_table: torch.Tensor, topk_indices: torch.Tensor) -> None:
+    dev = q_index_fp8.device
+    _require(dev.type == "cuda", "tensors must be on a CUDA device")
+    for name, t in (("k_index_cache_fp8", k_index_cache_fp8), ("weights", weights),
+                    ("seq_lens", seq_lens), ("block_table", block_table),
+                    ("topk_indices", topk_indices)):
+        _require(t.device == dev, f"{name} is on {t.device}, expected {dev}")
+    _require(q_index_fp8.dtype == torch.float8_e4m3fn,
+             f"q_index_fp8 must be float8_e4m3fn, got {q_index_fp8.dtype}")
+    _require(q_index_fp8.dim() == 3 and tuple(q_index_fp8.shape[1:]) == (NUM_HEADS, HEAD_DIM),
+             f"q_index_fp8 must be [B, {NUM_HEADS}, {HEAD_DIM}], got {tuple(q_index_fp8.shape)}")
+    B = q_index_fp8.shape[0]
+    _require(weights.dtype == torch.float32 and tuple(weights.shape) == (B, NUM_HEADS),
+             f"weights must be float32 [{B}, {NUM_HEADS}]")
+    _require(seq_lens.dtype == torch.int32 and tuple(seq_lens.shape) == (B,),
+             f"seq_lens must be int32 [{B}]")
+    _require(block_table.dim() == 2 and block_table.shape[0] == B and block_table.shape[1] >= 1,
+             f"block_table must be [{B}, max_pages]")
+    _require(block_table.dtype in (torch.int32, torch.int64), "block_table must be int32 or int64")
+    _require(topk_indices.dtype == torch.int32 and tuple(topk_indices.shape) == (B, TOPK),
+             f"topk_indices must be int32 [{B}, {TOPK}]")
+    _require(topk_indices.is_contiguous(), "topk_indices must be contiguous (written in place)")
+    num_pages = num_pages_of(k_index_cache_fp8)
+    if B == 0:
+        return
+    # The reference calls .contiguous() on every input (kernel.py:365-368)
+    # and converts the block table to int32 (kernel.py:210).
+    q = q_index_fp8.contiguous()
+    k = k_index_cache_fp8.contiguous()
+    w = weights.contiguous()
+    sl = seq_lens.contiguous()
+    bt = block_table.to(torch.int32).contiguous()
+    max_pages = bt.shape[1]
+
+    L = _native.lib()
+    nbytes = L.dsa_indexer_workspace_bytes(B, max_pages)
+    cur = torch.cuda.current_stream(dev).cuda_stream
+    ws = workspace.get(dev, "indexer", nbytes, cur)
+    stream = ctypes.c_void_p(cur)
+    with torch.cuda.device(dev):
+        st = L.dsa_indexer_run(_ptr(q), _ptr(k), num_pages, _ptr(w), _ptr(sl), _ptr(bt), B,
+                               max_pages, _ptr(topk_indices), _ptr(ws), ws.numel(), stream)
+    _native.check(st, "dsa_indexer_run")
+    if _CHECK and not torch.cuda.is_current_stream_capturing():
+        raise_on_device_status(dev)
+
+
+def device_status(device: torch.device, clear: bool = True) -> int:
+    """OR of the sticky device status bits of every indexer workspace on
+    `device` (synchronises)."""
+    bits = 0
+    stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    for ws in workspace.buffers_of(device, "indexer"):
+        out = ctypes.c_uint32(0)
+        with torch.cuda.device(device):
+            st = _native.lib().dsa_read_device_status(_ptr(ws), ctypes.byref(out), int(clear),
+                                                      stream)
+        _native.check(st, "dsa_read_device_status")
+        bits |= int(out.value)
+    return bits
+
+
+def raise_on_device_status(device: torch.device) -> None:
+    bits = device_status(device, clear=True)
+    if bits:
+        raise _native.DsaError(f"dsa_indexer: {_native.describe_device_status(bits)} "
+                               f"(status bits {bits:#x})")

@@ -1,0 +1,36 @@
+"""Request sharding for data-parallel DSA decode on one node.
+
+Decode requests are independent, so a batch is split by request across the
+GPUs; each GPU holds its own page pools (FP8 index cache, ckv, kpe) and block
+table for its requests, and no collective runs on the hot path.  The split
+balances context tokens (the indexer's work is 132 B per token, attention's
+is fixed per request): requests are assigned longest-first to the rank with
+the fewest tokens so far (LPT), ties to the lower rank, and each rank keeps
+its requests in their original order.
+"""
+
+from __future__ import annotations
+
+
+def shard_requests(seq_lens: list, world: int) -> list:
+    """Returns one list of request indices per rank."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    load = [0] * world
+    count = [0] * world
+    shards = [[] for _ in range(world)]
+    order = sorted(range(len(seq_lens)), key=lambda i: (-int(seq_lens[i]), i))
+    for i in order:
+        # token load, then request count (attention work), then rank id
+        r = min(range(world), key=lambda k: (load[k], count[k], k))
+        shards[r].append(i)
+        load[r] += max(0, int(seq_lens[i]))
+        count[r] += 1
+    return [sorted(s) for s in shards]
+
+
+def shard_imbalance(seq_lens: list, shards: list) -> float:
+    """max rank tokens / mean rank tokens (1.0 = perfect)."""
+    loads = [sum(max(0, int(seq_lens[i])) for i in s) for s in shards]
+    mean = sum(loads) / max(1, len(loads))
+    return max(loads) / mean if mean > 0 else 1.0

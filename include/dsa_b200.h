@@ -1,0 +1,144 @@
+/*
+ * dsa_b200.h -- C ABI of the B200 (sm_100a) DSA decode kernels.
+ *
+ * Two operators, both destination-passing style (the caller owns inputs,
+ * outputs and the scratch workspace; nothing here allocates device memory):
+ *
+ *   dsa_indexer_run    -- FP8 lightning indexer + top-2048 select.
+ *     Replaces the reference entry point
+ *       run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table,
+ *           topk_indices)
+ *     at dsa_indexer/solution/triton/kernel.py:364-436 and its host driver
+ *     dsa_topk_run_ms (kernel.py:190-319).
+ *
+ *   dsa_attention_run  -- sparse MLA attention over the selected slots.
+ *     Replaces the reference entry point
+ *       run(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale,
+ *           output, lse)
+ *     at dsa_attention/solution/triton/kernel.py:240-252 and its host driver
+ *     dsa_sparse_attention (kernel.py:174-218).
+ *
+ * All pointers are device pointers except where stated; all launches go to
+ * `stream` (a cudaStream_t passed as void*), so calls are CUDA-graph
+ * capturable.  No call synchronises the device or reads device memory on the
+ * host (unlike the reference indexer, which reads seq_lens on the host at
+ * kernel.py:375).
+ *
+ * Every function returns a dsa_status (0 == DSA_OK).  Argument errors are
+ * detected on the host before anything is launched.  Data-dependent errors
+ * (a page id outside the pool, a seq_len larger than the block table, a
+ * sparse index outside the cache, a bounded wait that ran out) are recorded
+ * by the kernels as bits of a sticky 32-bit word at the start of the
+ * workspace; dsa_read_device_status() reads and optionally clears it.
+ */
+#ifndef DSA_B200_H_
+#define DSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSA_API __attribute__((visibility("default")))
+#else
+#define DSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (host side) ---------------------------------------- */
+#define DSA_OK                       0
+#define DSA_ERR_INVALID_ARGUMENT     1
+#define DSA_ERR_MISALIGNED           2
+#define DSA_ERR_WORKSPACE_TOO_SMALL  3
+#define DSA_ERR_CUDA                 4
+#define DSA_ERR_UNSUPPORTED_DEVICE   5
+#define DSA_ERR_TENSOR_MAP           6
+
+/* ---- sticky device status bits (first uint32 of each workspace) ------ */
+#define DSA_DEV_BAD_SEQ_LEN   0x1u  /* seq_len < 0 or > max_pages*64; clamped   */
+#define DSA_DEV_BAD_PAGE      0x2u  /* block_table entry outside [0, num_pages) */
+#define DSA_DEV_BAD_INDEX     0x4u  /* sparse index outside [-1, num_slots)     */
+#define DSA_DEV_WAIT_TIMEOUT  0x8u  /* a bounded pipeline wait gave up          */
+
+/* Shape constants of the two contest definitions
+ * dsa_topk_indexer_fp8_h64_d128_topk2048_ps64 and
+ * dsa_sparse_attention_h16_ckv512_kpe64_topk2048_ps64. */
+#define DSA_PAGE_SIZE        64
+#define DSA_INDEX_HEADS      64
+#define DSA_INDEX_DIM        128
+#define DSA_INDEX_PAGE_BYTES 8448  /* 64*128 fp8 + 64 fp32 scales (kernel.py:80) */
+#define DSA_TOPK             2048
+#define DSA_ATTN_HEADS       16
+#define DSA_CKV_DIM          512
+#define DSA_KPE_DIM          64
+
+/* Version of this ABI (bumped on any signature change). */
+DSA_API int dsa_b200_abi_version(void);
+
+/* Human-readable text for a dsa_status value; never NULL. */
+DSA_API const char* dsa_b200_status_string(int status);
+
+/* Bytes of device workspace dsa_indexer_run needs for this batch and block
+ * table width (256-byte header + fp32 score rows). */
+DSA_API size_t dsa_indexer_workspace_bytes(int32_t batch, int32_t max_pages);
+
+/* FP8 lightning indexer, decode (one query token per request).
+ *
+ *   q_index_fp8       [batch, 64, 128] float8_e4m3fn, contiguous
+ *   k_index_cache_fp8 num_pages pages of 8448 bytes: 64x128 fp8 then 64 fp32
+ *                     scales (the [num_pages, 64, 1, 132] uint8 cache viewed
+ *                     as bytes), 16-byte aligned
+ *   weights           [batch, 64] fp32
+ *   seq_lens          [batch] int32 (device memory; never read on the host)
+ *   block_table       [batch, max_pages] int32
+ *   topk_indices      [batch, 2048] int32 output: global slot ids
+ *                     block_table[b, t/64]*64 + t%64 of the top-min(L,2048)
+ *                     tokens, score descending, ties by lower token index,
+ *                     then -1 padding.
+ *
+ * Mirrors dsa_indexer/solution/triton/kernel.py:364 (argument order and
+ * meaning), plus the sizes a C caller must pass explicitly. */
+DSA_API int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cache_fp8,
+                    int64_t num_pages, const float* weights,
+                    const int32_t* seq_lens, const int32_t* block_table,
+                    int32_t batch, int32_t max_pages, int32_t* topk_indices,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of device workspace dsa_attention_run needs for num_tokens queries
+ * on this device (256-byte header + split-softmax partial records). */
+DSA_API size_t dsa_attention_workspace_bytes(int32_t num_tokens);
+
+/* Sparse MLA attention, one query token per row of sparse_indices.
+ *
+ *   q_nope          [num_tokens, 16, 512] bf16
+ *   q_pe            [num_tokens, 16, 64]  bf16
+ *   ckv_cache       num_slots rows of 512 bf16 ([pages, 64, 512] flattened)
+ *   kpe_cache       num_slots rows of 64 bf16  ([pages, 64, 64] flattened)
+ *   sparse_indices  [num_tokens, 2048] int32 global slot ids, -1 = padding
+ *   output          [num_tokens, 16, 512] bf16
+ *   lse             [num_tokens, 16] fp32, base-2 log-sum-exp of the scaled
+ *                   logits; -inf (and output 0) for a row with no valid index
+ *
+ * Mirrors dsa_attention/solution/triton/kernel.py:241 (argument order and
+ * meaning), plus the sizes a C caller must pass explicitly. */
+DSA_API int dsa_attention_run(const void* q_nope, const void* q_pe,
+                      const void* ckv_cache, const void* kpe_cache,
+                      int64_t num_slots, const int32_t* sparse_indices,
+                      int32_t num_tokens, float sm_scale,
+                      void* output, float* lse,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Copies the sticky device status word of `workspace` to *status_out
+ * (synchronising `stream`), and zeroes it when `clear` is non-zero.
+ * No counterpart in the reference, which has no error channel
+ * (errors there surface as Python exceptions, FAQ.md:238-240). */
+DSA_API int dsa_read_device_status(void* workspace, uint32_t* status_out, int clear,
+                           void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* DSA_B200_H_ */

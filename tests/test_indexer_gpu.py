@@ -1,0 +1,192 @@
+"""GPU parity of the indexer (dsa_b200.indexer.run -> C ABI -> sm_100a
+kernels) against the CPU oracle and the golden fixture."""
+
+import pathlib
+
+import numpy as np
+import pytest
+import torch
+
+from dsa_b200 import DsaError, indexer, workloads
+from dsa_b200 import workspace as ws_mod
+from oracle import compare
+from oracle import indexer as oix
+
+pytestmark = pytest.mark.gpu
+GOLD = pathlib.Path(__file__).resolve().parent / "golden"
+
+
+def run_gpu(ix, out=None):
+    B = ix.q_index_fp8.shape[0]
+    if out is None:
+        out = torch.full((B, 2048), 7, dtype=torch.int32, device=ix.q_index_fp8.device)
+    indexer.run(ix.q_index_fp8, ix.k_index_cache_fp8, ix.weights, ix.seq_lens, ix.block_table, out)
+    torch.cuda.synchronize()
+    return out
+
+
+def oracle_check(ix, got, rows=None):
+    """Compares `got` with the oracle on `rows` (all by default)."""
+    rows = list(range(ix.q_index_fp8.shape[0])) if rows is None else rows
+    q = ix.q_index_fp8[rows].cpu()
+    kc = ix.k_index_cache_fp8.cpu()
+    w = ix.weights[rows].cpu()
+    sl = ix.seq_lens[rows].cpu()
+    bt = ix.block_table[rows].cpu()
+    ref, scores = oix.indexer_reference(q, kc, w, sl, bt)
+    ku = kc.view(torch.uint8).reshape(-1)
+    bounds = [oix.score_error_bound(q[i], ku, w[i], int(sl[i]), bt[i].long())
+              for i in range(len(rows))]
+    rep = compare.compare_topk(got[rows].cpu(), ref, scores, bounds, sl, bt, kc.shape[0])
+    assert rep.ok, rep.problems[:5]
+    return rep
+
+
+@pytest.mark.parametrize("seq_lens", [
+    [100], [2048], [2049], [1, 63, 64, 65, 127, 128, 129], [2500, 130, 0, 71], [0, 0, 0],
+])
+def test_small_lengths(cuda_device, seq_lens):
+    ix = workloads.make_indexer_inputs(seq_lens, pool_pages=64, seed=sum(seq_lens) + 1,
+                                       device=cuda_device)
+    got = run_gpu(ix)
+    rep = oracle_check(ix, got)
+    assert rep.swaps == 0
+
+
+def test_config0_batch8(cuda_device):
+    g = torch.Generator().manual_seed(0)
+    lens = workloads.uniform_lengths(8, 2048, 8192, g)
+    ix = workloads.make_indexer_inputs(lens, pool_pages=1024, seed=0, device=cuda_device)
+    got = run_gpu(ix)
+    rep = oracle_check(ix, got)
+    print(f"config0: exact rows {rep.exact_rows}/8, boundary swaps {rep.swaps}")
+
+
+def test_golden_fixture(cuda_device):
+    z = np.load(GOLD / "indexer_small.npz")
+    ix = workloads.IndexerInputs(
+        torch.from_numpy(z["q"]).view(torch.float8_e4m3fn).to(cuda_device),
+        torch.from_numpy(z["k_cache"]).to(cuda_device),
+        torch.from_numpy(z["weights"]).to(cuda_device),
+        torch.from_numpy(z["seq_lens"]).to(cuda_device),
+        torch.from_numpy(z["block_table"]).to(cuda_device))
+    got = run_gpu(ix).cpu()
+    gold = torch.from_numpy(z["topk"])
+    for b in range(gold.shape[0]):
+        L = int(z["seq_lens"][b])
+        k = min(L, 2048)
+        assert set(got[b, :k].tolist()) == set(gold[b, :k].tolist()), b
+        assert (got[b, k:] == -1).all()
+    oracle_check(ix, got.to(cuda_device))
+
+
+def test_all_equal_scores_break_ties_by_index(cuda_device):
+    # q == 0 makes every score 0: the top-2048 are the first 2048 tokens, in
+    # token order.  L > the shared-memory candidate capacity exercises the
+    # global fallback of the select.
+    for L in (5000, 100000):
+        ix = workloads.make_indexer_inputs([L], pool_pages=L // 64 + 2, seed=3, device=cuda_device)
+        ix.q_index_fp8.zero_()
+        got = run_gpu(ix).cpu()[0]
+        bt = ix.block_table.cpu()[0].long()
+        tok = torch.arange(2048)
+        want = (bt[tok // 64] * 64 + tok % 64).to(torch.int32)
+        assert torch.equal(got, want), L
+
+
+def test_repeated_page_ties(cuda_device):
+    # Every page of the request is the same physical page: 64 distinct
+    # scores, each repeated L/64 times -> ties resolved by token index.
+    L = 8192
+    ix = workloads.make_indexer_inputs([L], pool_pages=16, seed=5, device=cuda_device)
+    ix.block_table.fill_(3)
+    got = run_gpu(ix)
+    rep = oracle_check(ix, got)
+    assert rep.exact_rows == 1
+
+
+def test_longer_block_table_and_minus_one_tail(cuda_device):
+    lens = [3000, 700]
+    ix = workloads.make_indexer_inputs(lens, pool_pages=128, seed=9, device=cuda_device,
+                                       max_pages=100)
+    bt = ix.block_table.clone()
+    bt[0, 47:] = -1   # beyond ceil(3000/64) = 47 pages: never read
+    bt[1, 11:] = -1
+    ix.block_table = bt
+    got = run_gpu(ix)
+    oracle_check(ix, got)
+
+
+def test_bad_page_id_is_reported(cuda_device):
+    ix = workloads.make_indexer_inputs([300], pool_pages=16, seed=11, device=cuda_device)
+    ix.block_table[0, 2] = 10_000
+    with pytest.raises(DsaError, match="block_table"):
+        run_gpu(ix)
+
+
+def test_bad_seq_len_is_reported(cuda_device):
+    ix = workloads.make_indexer_inputs([300], pool_pages=16, seed=12, device=cuda_device)
+    ix.seq_lens[0] = ix.block_table.shape[1] * 64 + 1
+    with pytest.raises(DsaError, match="seq_len"):
+        run_gpu(ix)
+
+
+def test_graph_capture_reads_seq_lens_on_device(cuda_device):
+    lens = [4000, 2500, 9000]
+    ix = workloads.make_indexer_inputs(lens, pool_pages=512, seed=21, device=cuda_device,
+                                       max_pages=160)
+    out = torch.empty(3, 2048, dtype=torch.int32, device=cuda_device)
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):  # warm-up on the capture stream sizes its workspace
+        run_gpu(ix, out)
+    with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+        indexer.run(ix.q_index_fp8, ix.k_index_cache_fp8, ix.weights, ix.seq_lens,
+                    ix.block_table, out)
+    torch.cuda.current_stream().wait_stream(s)
+    for new in ([4000, 2500, 9000], [10000, 64, 2049], [0, 5000, 1]):
+        ix.seq_lens.copy_(torch.tensor(new, dtype=torch.int32))
+        g.replay()
+        torch.cuda.synchronize()
+        oracle_check(ix, out.clone())
+
+
+def test_score_precision_vs_oracle(cuda_device):
+    # The fp32 scores live in the workspace after a call; their deviation from
+    # the oracle must stay inside the reordering bound the comparator uses.
+    lens = [6000, 3000]
+    ix = workloads.make_indexer_inputs(lens, pool_pages=256, seed=31, device=cuda_device)
+    run_gpu(ix)
+    stream_id = torch.cuda.current_stream(cuda_device).cuda_stream
+    buf = ws_mod.all_buffers()[(cuda_device.index, "indexer", stream_id)]
+    stride = ix.block_table.shape[1] * 64
+    scores = buf[256:256 + 4 * 2 * stride].view(torch.float32).reshape(2, stride).cpu()
+    q, kc, w = ix.q_index_fp8.cpu(), ix.k_index_cache_fp8.cpu(), ix.weights.cpu()
+    bt = ix.block_table.cpu()
+    ku = kc.view(torch.uint8).reshape(-1)
+    worst = 0.0
+    for b, L in enumerate(lens):
+        ref = oix.score_request(q[b], ku, w[b], L, bt[b].long())
+        bound = oix.score_error_bound(q[b], ku, w[b], L, bt[b].long())
+        ratio = float(((scores[b, :L] - ref).abs() / bound).max())
+        worst = max(worst, ratio)
+    print(f"max |gpu - oracle| / bound = {worst:.3g}")
+    assert worst <= 1.0
+
+
+def test_long_context_config2(cuda_device):
+    g = torch.Generator().manual_seed(2)
+    lens = workloads.uniform_lengths(64, 32768, 131072, g)
+    ix = workloads.make_indexer_inputs(lens, pool_pages=150_000, seed=2, device=cuda_device)
+    got = run_gpu(ix)
+    rep = oracle_check(ix, got, rows=[0, 17, 63])
+    # Size-independent properties on every row: 2048 distinct slots, each in
+    # one of the request's pages.
+    bt = ix.block_table.cpu()
+    for b in range(64):
+        row = got[b].cpu()
+        assert (row >= 0).all() and row.unique().numel() == 2048, b
+        pages = set(bt[b, : (lens[b] + 63) // 64].tolist())
+        assert set((row // 64).tolist()) <= pages, b
+    print(f"config2 sample: exact {rep.exact_rows}/3, swaps {rep.swaps}")
