@@ -52,13 +52,19 @@ def parse_args():
     ap.add_argument("--streams", type=int, default=1, help="streams inside the captured step")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="requests per GPU (overrides the workload's batch; north_star shape)")
+    ap.add_argument("--seq-len", type=int, default=65536, help="context length with --batch")
     return ap.parse_args()
 
 
-def workload_lengths(name: str, rank: int, world: int) -> tuple:
+def workload_lengths(name: str, rank: int, world: int, batch: int = 0,
+                     seq_len: int = 65536) -> tuple:
     """(this rank's seq_lens, total requests, description)."""
     from dsa_b200 import sharding, workloads
 
+    if batch > 0:
+        return [seq_len] * batch, batch * world, f"{batch} requests/GPU x {seq_len}-token context"
     if name == "north_star":
         return [65536] * 64, 64 * world, "64 requests/GPU x 65536-token context"
     g = torch.Generator().manual_seed(4)
@@ -204,7 +210,7 @@ def run_reference(args, rank: int, world: int) -> int:
     from oracle import indexer as oix
 
     torch.set_num_threads(os.cpu_count() or 1)
-    lens, total_req, desc = workload_lengths(args.workload, 0, world)
+    lens, total_req, desc = workload_lengths(args.workload, 0, world, args.batch, args.seq_len)
     L = lens[0]
     dec = workloads.make_decode_inputs([L], seed=77, device="cpu")
     ix = dec.indexer
@@ -257,7 +263,7 @@ def main() -> int:
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    lens, total_req, desc = workload_lengths(args.workload, rank, world)
+    lens, total_req, desc = workload_lengths(args.workload, rank, world, args.batch, args.seq_len)
     dec = workloads.make_decode_inputs(lens, seed=1000 + rank, device=dev)
     step = pipeline.DecodeStep(dec, use_graph=True, streams=args.streams)
     ix_bytes = workloads.indexer_bytes(lens)
@@ -326,7 +332,7 @@ def main() -> int:
     at_gbs = at_bytes / (at_ms * 1e-3) / 1e9
     traffic = profiled_traffic("indexer_score_kernel", args.workload)
     cpu = None
-    if world == 1:
+    if world == 1 and args.cpu_seconds > 0:
         cpu = cpu_oracle_sample(dec, step.topk, args.cpu_seconds)
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K,

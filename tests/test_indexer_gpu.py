@@ -98,7 +98,7 @@ def test_repeated_page_ties(cuda_device):
     # Every page of the request is the same physical page: 64 distinct
     # scores, each repeated L/64 times -> ties resolved by token index.
     L = 8192
-    ix = workloads.make_indexer_inputs([L], pool_pages=16, seed=5, device=cuda_device)
+    ix = workloads.make_indexer_inputs([L], pool_pages=160, seed=5, device=cuda_device)
     ix.block_table.fill_(3)
     got = run_gpu(ix)
     rep = oracle_check(ix, got)
