@@ -10,17 +10,22 @@
 //   T x 32 tiles of 64 selected rows; CTA c takes the contiguous slice
 //   [c*U/G, (c+1)*U/G) ("stream-K"), so every SM streams the same number of
 //   rows whatever T is.  Roles:
-//     warp 0     producer: reads 64 slot ids, TMA tile::gather4 of the rows'
-//                ckv (8 x 128-byte chunks) and kpe (1 chunk) into a 2-deep
-//                ring with 128-byte swizzle; q_nope/q_pe of the token by
-//                2-D TMA when the token changes.
-//     warp 1     MMA issuer (tcgen05, bf16, fp32 accumulators in TMEM):
+//     warps 0-3  producers: read the tile's 64 slot ids (one tile ahead) and
+//                TMA tile::gather4 the rows' ckv (8 x 128-byte chunks) and
+//                kpe (1 chunk) into a 2-deep ring with 128-byte swizzle.  A
+//                warp issues gather4 ops at a fixed rate, so the 9 chunks are
+//                split over 4 warps (measured: 1 issuing warp caps random-row
+//                gathers near 2 TB/s, 8 warps reach the HBM roofline).
+//                Warp 0 also loads q_nope / q_pe by 2-D TMA per token.
+//     warp 4     MMA issuer (tcgen05, bf16, fp32 accumulators in TMEM),
+//                issuing logits and PV in whatever order their inputs
+//                become ready:
 //                  S^T[64 rows, 16 heads]  = K[64, 576] . Q[16, 576]^T
 //                  (M = 64, N = 16, 36 x K16), then after the softmax
 //                  O^T[512, 16] += V^T[512, 64] . P^T[64, 16]
 //                  (4 x M = 128, N = 16, 4 x K16); V^T is the same shared
 //                  memory as the ckv chunks, read MN-major.
-//     warps 2-5  online softmax in base 2 with lazy rescaling (the running
+//     warps 5-8  online softmax in base 2 with lazy rescaling (the running
 //                max is only moved when a tile exceeds it by more than 8,
 //                so O in TMEM is rarely touched), P^T written as bf16.
 //   A token fully covered by one CTA is normalised and written directly;
@@ -51,7 +56,10 @@ constexpr int kStageBytes = kChunks * kChunkBytes;  // 73728
 constexpr int kQChunkBytes = kHeads * 128;       // 2048
 constexpr int kQBytes = kChunks * kQChunkBytes;  // 18432
 constexpr int kPBytes = kHeads * kRows * 2;      // 2048
-constexpr int kThreads = 192;
+constexpr int kProdWarps = 4;                    // warps 0-3: gather producers
+constexpr int kMmaWarp = 4;                      // warp 4: TMEM owner + MMA issuer
+constexpr int kSoftWarp0 = 5;                    // warps 5-8: online softmax
+constexpr int kThreads = 288;
 constexpr int kTmemCols = 256;
 constexpr uint32_t kColO = 0;    // O^T buffers at [0,64) and [64,128): 4 blocks x 16 heads
 constexpr uint32_t kColS = 128;  // S^T buffers at [128,144) and [144,160)
@@ -133,7 +141,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
 
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_full[s], kProdWarps); mbar_init(&kv_empty[s], 1);
       mbar_init(&q_full[s], 1);  mbar_init(&q_empty[s], 1);
       mbar_init(&s_full[s], 1);  mbar_init(&s_empty[s], 128);
       mbar_init(&p_full[s], 1);  mbar_init(&p_empty[s], 1);
@@ -148,7 +156,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     prefetch_tensor_map(&ckv_map); prefetch_tensor_map(&kpe_map);
     prefetch_tensor_map(&qn_map);  prefetch_tensor_map(&qp_map);
   }
-  if (warp == 1) tmem_alloc(tmem_base_smem, kTmemCols);
+  if (warp == kMmaWarp) tmem_alloc(tmem_base_smem, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -161,15 +169,30 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   const int t_first = static_cast<int>(u0 / kTilesPerTok);
   const WaitCtx wctx{abort_flag, p.status};
 
-  if (warp == 0) {
-    // ------------------------------------------------------ producer warp
+  if (warp < kProdWarps) {
+    // ------------------------------------------------------ producer warps
+    // Warp w gathers chunks w, w+4, w+8 (ckv 0-7, kpe 8) of every tile.
+    const int nchunks = (kChunks - warp + kProdWarps - 1) / kProdWarps;
     const uint64_t policy = make_policy_evict_first();
     int nq = 0, i = 0;
+    auto load_idx = [&](int j, int& a, int& b) {
+      a = b = 0;
+      if (j < n) {
+        const int64_t u = u0 + j;
+        const int32_t* r = p.indices + (u / kTilesPerTok) * kTopK + (u % kTilesPerTok) * kRows;
+        a = __ldg(r + 2 * lane);
+        b = __ldg(r + 2 * lane + 1);
+      }
+    };
+    int v0, v1;
+    load_idx(0, v0, v1);
     for (; i < n; ++i) {
       const int64_t u = u0 + i;
       const int t = static_cast<int>(u / kTilesPerTok);
       const int tile = static_cast<int>(u % kTilesPerTok);
-      if (i == 0 || tile == 0) {
+      int nv0, nv1;
+      load_idx(i + 1, nv0, nv1);  // next tile's slot ids, in flight meanwhile
+      if (warp == 0 && (i == 0 || tile == 0)) {
         const int slot = nq & 1;
         int ok = 1;
         if (lane == 0) {
@@ -186,89 +209,118 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
         ++nq;
       }
       const int s = i & 1;
-      const int32_t* idx_row = p.indices + static_cast<int64_t>(t) * kTopK + tile * kRows;
-      const int v0 = sanitize_slot(__ldg(idx_row + 2 * lane), p.num_slots, p.status);
-      const int v1 = sanitize_slot(__ldg(idx_row + 2 * lane + 1), p.num_slots, p.status);
+      const int r0v = sanitize_slot(v0, p.num_slots, p.status);
+      const int r1v = sanitize_slot(v1, p.num_slots, p.status);
       int ok = 1;
       if (lane == 0) {
         ok = mbar_wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, wctx);
-        if (ok) mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
+        if (ok) mbar_arrive_expect_tx(&kv_full[s], nchunks * 16 * 512);
       }
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       const int src = 2 * (lane & 15);
-      const int r0 = __shfl_sync(0xffffffffu, v0, src);
-      const int r1 = __shfl_sync(0xffffffffu, v1, src);
-      const int r2 = __shfl_sync(0xffffffffu, v0, src + 1);
-      const int r3 = __shfl_sync(0xffffffffu, v1, src + 1);
+      const int r0 = __shfl_sync(0xffffffffu, r0v, src);
+      const int r1 = __shfl_sync(0xffffffffu, r1v, src);
+      const int r2 = __shfl_sync(0xffffffffu, r0v, src + 1);
+      const int r3 = __shfl_sync(0xffffffffu, r1v, src + 1);
       if (lane < 16) {
         uint8_t* dst = stage_mem + s * kStageBytes + lane * 512;
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          tma_gather4(dst + c * kChunkBytes, &ckv_map, &kv_full[s], c * 64, r0, r1, r2, r3, policy);
-        tma_gather4(dst + 8 * kChunkBytes, &kpe_map, &kv_full[s], 0, r0, r1, r2, r3, policy);
+        for (int c = warp; c < kChunks; c += kProdWarps) {
+          if (c < 8)
+            tma_gather4(dst + c * kChunkBytes, &ckv_map, &kv_full[s], c * 64, r0, r1, r2, r3, policy);
+          else
+            tma_gather4(dst + c * kChunkBytes, &kpe_map, &kv_full[s], 0, r0, r1, r2, r3, policy);
+        }
       }
       __syncwarp();
+      v0 = nv0;
+      v1 = nv1;
     }
     if (lane == 0) {  // let in-flight copies land before the CTA can exit
       for (int k = (i > 2 ? i - 2 : 0); k < i; ++k) mbar_drain(&kv_full[k & 1], (k >> 1) & 1);
-      for (int k = (nq > 2 ? nq - 2 : 0); k < nq; ++k) mbar_drain(&q_full[k & 1], (k >> 1) & 1);
+      if (warp == 0)
+        for (int k = (nq > 2 ? nq - 2 : 0); k < nq; ++k) mbar_drain(&q_full[k & 1], (k >> 1) & 1);
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------ MMA issuer
+    // Logits of tile i need its gathered rows, its token's Q and a free S
+    // buffer; PV of tile i needs P(i) (and, at a segment start, a drained O
+    // buffer).  Both are polled and issued as soon as ready, so PV(i) never
+    // waits behind the next tile's gather.
     if (lane == 0 && n > 0) {
-      int sg = -1;
-      int prev_sg = 0;
-      bool prev_start = false;
-      bool ok = true;
-      auto issue_pv = [&](int j, int seg, bool seg_start) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&p_full[s], (j >> 1) & 1, wctx)) return false;
-        if (seg_start && !mbar_wait(&o_empty[seg & 1], ((seg >> 1) & 1) ^ 1, wctx)) return false;
-        tc_fence_after();
-        const uint32_t st = smem_u32(stage_mem + s * kStageBytes);
-        const uint32_t pb = smem_u32(p_mem + s * kPBytes);
-        const uint32_t obuf = tmem_base + kColO + 64u * (seg & 1);
+      // Descriptors of stage / Q / P buffer 0; buffer 1 is a fixed byte offset away.
+      const uint64_t st_desc0 = sdesc_sw128(smem_u32(stage_mem), 16, 1024);
+      const uint64_t v_desc0 = sdesc_sw128(smem_u32(stage_mem), kChunkBytes, 1024);
+      const uint64_t q_desc0 = sdesc_sw128(smem_u32(q_mem), 16, 1024);
+      const uint64_t p_desc0 = sdesc_sw128(smem_u32(p_mem), 16, 1024);
+      int nl = 0, np = 0;
+      unsigned long long t_idle = 0;
+      while (np < n) {
+        bool progressed = false;
+        if (nl < n) {
+          const int64_t u = u0 + nl;
+          const int tile = static_cast<int>(u % kTilesPerTok);
+          const int seg = static_cast<int>(u / kTilesPerTok) - t_first;
+          const bool seg_start = (nl == 0 || tile == 0);
+          const bool seg_end = (nl == n - 1 || tile == kTilesPerTok - 1);
+          const int s = nl & 1;
+          if ((!seg_start || mbar_test(&q_full[seg & 1], (seg >> 1) & 1)) &&
+              mbar_test(&kv_full[s], (nl >> 1) & 1) &&
+              mbar_test(&s_empty[s], ((nl >> 1) & 1) ^ 1)) {
+            tc_fence_after();
+            const uint64_t ad = st_desc0 + s * (kStageBytes >> 4);
+            const uint64_t bd = q_desc0 + (seg & 1) * (kQBytes >> 4);
+            const uint32_t d = tmem_base + kColS + 16u * s;
 #pragma unroll
-        for (int mb = 0; mb < 4; ++mb) {
-#pragma unroll
-          for (int kk = 0; kk < kRows / 16; ++kk) {
-            const uint64_t ad = sdesc_sw128(st + (2 * mb) * kChunkBytes + kk * 2048, kChunkBytes, 1024);
-            const uint64_t bd = sdesc_sw128(pb + kk * 32, 16, 1024);
-            umma_bf16(obuf + 16 * mb, ad, bd, kIdescO, (seg_start && kk == 0) ? 0u : 1u);
+            for (int k = 0; k < kChunks * 4; ++k) {
+              // +8192 bytes per 64-column chunk, +32 bytes per K16 step (>> 4)
+              umma_bf16(d, ad + (k >> 2) * (kChunkBytes >> 4) + (k & 3) * 2,
+                        bd + (k >> 2) * (kQChunkBytes >> 4) + (k & 3) * 2, kIdescS, k > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[s]);
+            if (seg_end) umma_commit(&q_empty[seg & 1]);
+            ++nl;
+            progressed = true;
           }
         }
-        umma_commit(&kv_empty[s]);
-        umma_commit(&p_empty[s]);
-        return true;
-      };
-      for (int i = 0; i < n && ok; ++i) {
-        const int64_t u = u0 + i;
-        const int tile = static_cast<int>(u % kTilesPerTok);
-        const bool seg_start = (i == 0 || tile == 0);
-        const bool seg_end = (i == n - 1 || tile == kTilesPerTok - 1);
-        if (seg_start) {
-          ++sg;
-          if (!mbar_wait(&q_full[sg & 1], (sg >> 1) & 1, wctx)) break;
+        if (np < nl) {
+          const int64_t u = u0 + np;
+          const int tile = static_cast<int>(u % kTilesPerTok);
+          const int seg = static_cast<int>(u / kTilesPerTok) - t_first;
+          const bool seg_start = (np == 0 || tile == 0);
+          const int s = np & 1;
+          if (mbar_test(&p_full[s], (np >> 1) & 1) &&
+              (!seg_start || mbar_test(&o_empty[seg & 1], ((seg >> 1) & 1) ^ 1))) {
+            tc_fence_after();
+            const uint32_t obuf = tmem_base + kColO + 64u * (seg & 1);
+#pragma unroll
+            for (int mb = 0; mb < 4; ++mb) {
+#pragma unroll
+              for (int kk = 0; kk < kRows / 16; ++kk) {
+                // V^T block mb: chunks 2mb, 2mb+1; K16 step = 16 rows = 2048 bytes
+                umma_bf16(obuf + 16 * mb,
+                          v_desc0 + s * (kStageBytes >> 4) + mb * (2 * kChunkBytes >> 4) + kk * (2048 >> 4),
+                          p_desc0 + s * (kPBytes >> 4) + kk * 2, kIdescO, (seg_start && kk == 0) ? 0u : 1u);
+              }
+            }
+            umma_commit(&kv_empty[s]);
+            umma_commit(&p_empty[s]);
+            ++np;
+            progressed = true;
+          }
         }
-        const int s = i & 1;
-        if (!mbar_wait(&kv_full[s], (i >> 1) & 1, wctx)) break;
-        if (!mbar_wait(&s_empty[s], ((i >> 1) & 1) ^ 1, wctx)) break;
-        tc_fence_after();
-        const uint32_t st = smem_u32(stage_mem + s * kStageBytes);
-        const uint32_t qb = smem_u32(q_mem + (sg & 1) * kQBytes);
-#pragma unroll 4
-        for (int k = 0; k < kChunks * 4; ++k) {
-          const uint32_t off = (k >> 2) * kChunkBytes + (k & 3) * 32;
-          const uint32_t qoff = (k >> 2) * kQChunkBytes + (k & 3) * 32;
-          umma_bf16(tmem_base + kColS + 16u * s, sdesc_sw128(st + off, 16, 1024),
-                    sdesc_sw128(qb + qoff, 16, 1024), kIdescS, k > 0 ? 1u : 0u);
+        if (progressed) {
+          t_idle = 0;
+        } else {
+          if (*abort_flag) break;
+          const unsigned long long now = global_timer_ns();
+          if (t_idle == 0) {
+            t_idle = now;
+          } else if (now - t_idle > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicOr(p.status, DSA_DEV_WAIT_TIMEOUT);
+            break;
+          }
         }
-        umma_commit(&s_full[s]);
-        if (seg_end) umma_commit(&q_empty[sg & 1]);
-        if (i > 0) ok = issue_pv(i - 1, prev_sg, prev_start);
-        prev_sg = sg;
-        prev_start = seg_start;
-        if (ok && i == n - 1) ok = issue_pv(i, sg, seg_start);
       }
       umma_commit(drain);
       mbar_drain(drain, 0);
@@ -279,7 +331,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     // that ANDs the threads' results, so the 128 threads always meet the same
     // barriers and leave the loop together if a wait gave up.
     const int sp = warp & 3;
-    const int e = tid - 64;              // 0..127
+    const int e = tid - 32 * kSoftWarp0; // 0..127
     const int h = e >> 3;                // head owned in the reduction phase
     const int g = e & 7;                 // 8-row group of that head
     const uint32_t lane_base = static_cast<uint32_t>(sp * 32) << 16;
@@ -437,7 +489,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }

@@ -8,9 +8,12 @@
 //    CTA c takes the contiguous slice [c*U/G, (c+1)*U/G) of the U tiles, so
 //    load balance does not depend on how seq_lens are distributed.  Roles:
 //      warp 0      TMA producer: raw FP8 pages (64 rows x 128 B, 128-byte
-//                  swizzle) straight from the paged cache into an 8-deep
-//                  shared-memory ring, and q[b] (64 heads x 128 B) when the
-//                  request changes.  Nothing is dequantised in HBM
+//                  swizzle) plus each page's 64 fp32 scales (bulk copy)
+//                  straight from the paged cache into an 8-deep shared-memory
+//                  ring, and q[b] (64 heads x 128 B) when the request changes.
+//                  The warp resolves the block-table entries of 32 tiles at a
+//                  time, one group ahead, so no load latency sits between
+//                  two TMA issues.  Nothing is dequantised in HBM
 //                  (the reference writes an fp32 copy of K, kernel.py:108-135).
 //      warp 1      MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 tokens,
 //                  N = 64 heads, K = 128 (4 x K32), fp32 accumulator in TMEM,
@@ -26,9 +29,12 @@
 // 2. topk_select_kernel (one CTA per request).  Exact top-min(L, 2048) by
 //    radix select on the 64-bit key (order(score) << 32 | ~token), which
 //    encodes "score descending, then lower token index first" as one total
-//    order.  Pass 1 histograms the top 11 key bits over all L scores; pass 2
-//    moves the winners of higher bins to the output and the boundary bin to
-//    a shared-memory candidate list, which later passes refine.  The 2048
+//    order.  The score kernel's epilogue already histograms the top 11 key
+//    bits per request (per-warp shared-memory histograms flushed into a
+//    global [batch, 2048] table, which the select kernel zeroes after use);
+//    one pass over the L scores then moves the winners of higher bins to the
+//    output and the boundary bin to a shared-memory candidate list, which
+//    later passes refine.  The 2048
 //    winners are bitonic-sorted and translated to global slot ids through
 //    the block table (kernel.py:156-169), then -1 padded (kernel.py:206).
 #include <mutex>
@@ -45,13 +51,17 @@ constexpr int kDim = DSA_INDEX_DIM;                       // 128 fp8 per token
 constexpr int kPageBytes = DSA_INDEX_PAGE_BYTES;          // 8448
 constexpr int kPageRows = kPageBytes / 128;               // page = 66 rows of 128 B
 constexpr int kPageDataBytes = kPage * kDim;              // 8192
+constexpr int kScaleBytes = kPage * 4;                    // 256
 constexpr int kTileTok = 2 * kPage;                       // 128 tokens per tile
-constexpr int kStageBytes = 2 * kPageDataBytes;           // 16384
+constexpr int kStageData = 2 * kPageDataBytes;            // 16384: two pages of FP8 rows
+constexpr int kStageStride = kStageData + 1024;           // + the two pages' scales, 1 KiB aligned
 constexpr int kStages = 8;
 constexpr int kAccStages = 4;
 constexpr int kTmemCols = kAccStages * kHeads;            // 256
 constexpr int kThreads = 192;
-constexpr int kMaxBatch = 8192;
+constexpr int kEpiWarps = 4;
+constexpr int kBins = 2048;                               // radix bins: top 11 key bits
+constexpr int kMaxBatch = 4096;
 constexpr int kMaxPagesPerSeq = 1 << 20;
 constexpr int64_t kMaxPool = (int64_t(1) << 31) / kPageRows - 1;
 
@@ -59,8 +69,9 @@ constexpr int64_t kMaxPool = (int64_t(1) << 31) / kPageRows - 1;
 constexpr uint32_t kIdesc = idesc_make(0, 0, false, false, 128, 64);
 
 constexpr int kOffStage = 0;
-constexpr int kOffQ = kOffStage + kStages * kStageBytes;          // 131072
-constexpr int kOffBar = kOffQ + 2 * kPageDataBytes;               // 147456
+constexpr int kOffQ = kOffStage + kStages * kStageStride;         // 139264
+constexpr int kOffHist = kOffQ + 2 * kPageDataBytes;              // 155648
+constexpr int kOffBar = kOffHist + kEpiWarps * kBins * 4;         // 188416
 constexpr int kNumBars = 2 * kStages + 4 + 2 * kAccStages + 1;
 constexpr int kOffMisc = kOffBar + 256;
 constexpr int kOffTiles = kOffMisc + 64;
@@ -75,12 +86,13 @@ struct ScoreParams {
   const float* weights;
   const int32_t* seq_lens;
   const int32_t* block_table;
-  float* scores;
+  float* scores;          // [batch][score_stride]
+  unsigned int* hist;     // [batch][kBins], zero on entry, cleared by the select kernel
   unsigned int* status;
   int64_t num_pages;
   int batch;
   int max_pages;
-  int score_stride;  // = max_pages * 64
+  int score_stride;       // = max_pages * 64
 };
 
 __device__ __forceinline__ int clamp_len(int L, int max_len, unsigned int* status) {
@@ -100,26 +112,44 @@ __device__ __forceinline__ int page_id(const ScoreParams& p, int b, int page_idx
   return pid;
 }
 
-// Walks the CTA's slice of the tile list: (request b, tile j within b).
-struct TileWalk {
-  const int* tile_off;
-  int batch;
-  int b;
-  int j;
-  __device__ void start(int64_t u) {
-    int lo = 0, hi = batch;  // find b with tile_off[b] <= u < tile_off[b+1]
-    while (lo < hi) {
-      int mid = (lo + hi) >> 1;
-      if (tile_off[mid + 1] <= u) lo = mid + 1; else hi = mid;
-    }
-    b = lo;
-    j = static_cast<int>(u - tile_off[b]);
+// Locates tile u of the work list: request b = the one with
+// tile_off[b] <= u < tile_off[b+1], tile j = u - tile_off[b].
+__device__ __forceinline__ void locate(const int* tile_off, int batch, int64_t u, int& b, int& j) {
+  int lo = 0, hi = batch;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (tile_off[mid + 1] <= u) lo = mid + 1; else hi = mid;
   }
-  __device__ void next() {
-    ++j;
-    while (b < batch && j >= tile_off[b + 1] - tile_off[b]) { ++b; j = 0; }
-  }
+  b = lo;
+  j = static_cast<int>(u - tile_off[b]);
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+// What the producer needs to know about one tile; each lane of the producer
+// warp resolves one tile of a 32-tile group so the block-table loads of a
+// whole group are in flight together (and one group ahead).
+struct TileInfo {
+  int b, j, npg, p0, p1;
 };
+
+__device__ __forceinline__ TileInfo tile_info(const ScoreParams& p, const int* tile_off,
+                                              int64_t u, int64_t u1, int max_len) {
+  TileInfo t{-1, 0, 0, 0, 0};
+  if (u < u1) {
+    locate(tile_off, p.batch, u, t.b, t.j);
+    const int L = clamp_len(__ldg(p.seq_lens + t.b), max_len, p.status);
+    const int req_pages = (L + kPage - 1) / kPage;
+    t.npg = (2 * t.j + 1 < req_pages) ? 2 : 1;
+    t.p0 = page_id(p, t.b, 2 * t.j);
+    t.p1 = t.npg == 2 ? page_id(p, t.b, 2 * t.j + 1) : 0;
+  }
+  return t;
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
 indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
@@ -129,6 +159,7 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* stage_mem = smem + kOffStage;
   uint8_t* q_mem = smem + kOffQ;
+  uint32_t* hist_all = reinterpret_cast<uint32_t*>(smem + kOffHist);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* full = bars;
   uint64_t* empty = bars + kStages;
@@ -148,15 +179,20 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   const int max_len = p.max_pages * kPage;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    // A stage is free again once its MMAs completed (1 commit) and every
+    // epilogue warp has read the stage's token scales (4 arrivals).
+    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + kEpiWarps); }
     for (int s = 0; s < 2; ++s) { mbar_init(&qfull[s], 1); mbar_init(&qempty[s], 1); }
-    for (int s = 0; s < kAccStages; ++s) { mbar_init(&accfull[s], 1); mbar_init(&accempty[s], 128); }
+    for (int s = 0; s < kAccStages; ++s) { mbar_init(&accfull[s], 1); mbar_init(&accempty[s], kEpiWarps); }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) { prefetch_tensor_map(&kmap); prefetch_tensor_map(&qmap); }
   if (warp == 1) tmem_alloc(tmem_base_smem, kTmemCols);
+  if (warp >= 2) {  // zero the per-warp histograms
+    for (int i = tid - 64; i < kEpiWarps * kBins; i += 128) hist_all[i] = 0;
+  }
 
   // Tile prefix sums over requests (each CTA recomputes them: seq_lens stay
   // on the device and B is small).
@@ -197,51 +233,67 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   const WaitCtx wctx{abort_flag, p.status};
 
   if (warp == 0) {
-    // ------------------------------------------------------ TMA producer
-    if (lane == 0 && u0 < u1) {
-      const uint64_t policy = make_policy_evict_first();
-      TileWalk w{tile_off, p.batch, 0, 0};
-      w.start(u0);
-      int cur_b = -1, nq = 0;
-      int64_t n = 0;
-      for (int64_t u = u0; u < u1; ++u, ++n, w.next()) {
-        if (w.b != cur_b) {
-          cur_b = w.b;
-          const int slot = nq & 1;
-          if (!mbar_wait(&qempty[slot], ((nq >> 1) & 1) ^ 1, wctx)) break;
-          mbar_arrive_expect_tx(&qfull[slot], kPageDataBytes);
-          tma_load_2d(q_mem + slot * kPageDataBytes, &qmap, &qfull[slot], 0, cur_b * kHeads);
-          ++nq;
+    // ------------------------------------------------------ TMA producer warp
+    const uint64_t policy = make_policy_evict_first();
+    int cur_b = -1, nq = 0;
+    int64_t n = 0;
+    bool ok = true;
+    TileInfo nxt = tile_info(p, tile_off, u0 + lane, u1, max_len);
+    for (int64_t g0 = u0; g0 < u1 && ok; g0 += 32) {
+      const TileInfo cur = nxt;
+      nxt = tile_info(p, tile_off, g0 + 32 + lane, u1, max_len);  // one group ahead
+      const int cnt = static_cast<int>(u1 - g0 < 32 ? u1 - g0 : 32);
+      for (int t = 0; t < cnt; ++t, ++n) {
+        const int b = __shfl_sync(0xffffffffu, cur.b, t);
+        const int npg = __shfl_sync(0xffffffffu, cur.npg, t);
+        const int p0 = __shfl_sync(0xffffffffu, cur.p0, t);
+        const int p1 = __shfl_sync(0xffffffffu, cur.p1, t);
+        int good = 1;
+        if (lane == 0) {
+          if (b != cur_b) {
+            const int slot = nq & 1;
+            good = mbar_wait(&qempty[slot], ((nq >> 1) & 1) ^ 1, wctx);
+            if (good) {
+              mbar_arrive_expect_tx(&qfull[slot], kPageDataBytes);
+              tma_load_2d(q_mem + slot * kPageDataBytes, &qmap, &qfull[slot], 0, b * kHeads);
+            }
+            ++nq;
+          }
+          const int s = static_cast<int>(n % kStages);
+          const uint32_t ph = static_cast<uint32_t>((n / kStages) & 1);
+          good = good && mbar_wait(&empty[s], ph ^ 1, wctx);
+          if (good) {
+            uint8_t* st = stage_mem + s * kStageStride;
+            mbar_arrive_expect_tx(&full[s], npg * (kPageDataBytes + kScaleBytes));
+            tma_load_2d_hint(st, &kmap, &full[s], 0, p0 * kPageRows, policy);
+            bulk_load(st + kStageData, p.k_cache + static_cast<int64_t>(p0) * kPageBytes + kPageDataBytes,
+                      kScaleBytes, &full[s]);
+            if (npg == 2) {
+              tma_load_2d_hint(st + kPageDataBytes, &kmap, &full[s], 0, p1 * kPageRows, policy);
+              bulk_load(st + kStageData + kScaleBytes,
+                        p.k_cache + static_cast<int64_t>(p1) * kPageBytes + kPageDataBytes,
+                        kScaleBytes, &full[s]);
+            }
+          }
         }
-        const int s = static_cast<int>(n % kStages);
-        const uint32_t ph = static_cast<uint32_t>((n / kStages) & 1);
-        if (!mbar_wait(&empty[s], ph ^ 1, wctx)) break;
-        const int L = clamp_len(__ldg(p.seq_lens + cur_b), max_len, p.status);
-        const int req_pages = (L + kPage - 1) / kPage;
-        const int npg = (2 * w.j + 1 < req_pages) ? 2 : 1;
-        mbar_arrive_expect_tx(&full[s], npg * kPageDataBytes);
-        for (int g = 0; g < npg; ++g) {
-          const int pid = page_id(p, cur_b, 2 * w.j + g);
-          tma_load_2d_hint(stage_mem + s * kStageBytes + g * kPageDataBytes, &kmap, &full[s], 0,
-                           pid * kPageRows, policy);
-        }
+        cur_b = b;
+        if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
       }
-      // Let every copy this thread issued land before the CTA can exit.
-      const int64_t issued = n;
-      for (int64_t k = (issued > kStages ? issued - kStages : 0); k < issued; ++k)
+    }
+    if (lane == 0) {  // let every copy this thread issued land before the CTA can exit
+      for (int64_t k = (n > kStages ? n - kStages : 0); k < n; ++k)
         mbar_drain(&full[k % kStages], static_cast<uint32_t>((k / kStages) & 1));
       for (int k = (nq > 2 ? nq - 2 : 0); k < nq; ++k) mbar_drain(&qfull[k & 1], (k >> 1) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------ MMA issuer
     if (lane == 0 && u0 < u1) {
-      TileWalk w{tile_off, p.batch, 0, 0};
-      w.start(u0);
-      int cur_b = -1, nq = 0, slot = 0;
+      int cur_b = -1, nq = 0, slot = 0, b = 0, j = 0;
+      locate(tile_off, p.batch, u0, b, j);
       int64_t n = 0;
-      for (int64_t u = u0; u < u1; ++u, ++n, w.next()) {
-        if (w.b != cur_b) {
-          cur_b = w.b;
+      for (int64_t u = u0; u < u1; ++u, ++n) {
+        if (b != cur_b) {
+          cur_b = b;
           if (nq > 0) umma_commit(&qempty[(nq - 1) & 1]);
           slot = nq & 1;
           if (!mbar_wait(&qfull[slot], (nq >> 1) & 1, wctx)) break;
@@ -254,48 +306,63 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         if (!mbar_wait(&full[s], ph, wctx)) break;
         if (!mbar_wait(&accempty[a], aph ^ 1, wctx)) break;
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(stage_mem + s * kStageBytes);
-        const uint32_t b_addr = smem_u32(q_mem + slot * kPageDataBytes);
+        const uint64_t ad = sdesc_sw128(smem_u32(stage_mem + s * kStageStride), 16, 1024);
+        const uint64_t bd = sdesc_sw128(smem_u32(q_mem + slot * kPageDataBytes), 16, 1024);
 #pragma unroll
-        for (int k = 0; k < kDim / 32; ++k) {
-          umma_f8(tmem_base + a * kHeads, sdesc_sw128(a_addr + 32 * k, 16, 1024),
-                  sdesc_sw128(b_addr + 32 * k, 16, 1024), kIdesc, k > 0 ? 1u : 0u);
-        }
+        for (int k = 0; k < kDim / 32; ++k)  // +32 bytes along K per step (start address >> 4)
+          umma_f8(tmem_base + a * kHeads, ad + 2 * k, bd + 2 * k, kIdesc, k > 0 ? 1u : 0u);
         umma_commit(&empty[s]);
         umma_commit(&accfull[a]);
+        if (++j == tile_off[b + 1] - tile_off[b]) {
+          j = 0;
+          do { ++b; } while (b < p.batch && tile_off[b + 1] == tile_off[b]);
+        }
       }
       umma_commit(drain);
       mbar_drain(drain, 0);
     }
   } else {
-    // ------------------------------------------------------ epilogue
+    // ------------------------------------------------------ epilogue warps
     const int sp = warp & 3;          // TMEM sub-partition this warp may access
     const int row = sp * 32 + lane;   // token row of the 128-token tile
+    uint32_t* hist = hist_all + (warp - 2) * kBins;
     if (u0 < u1) {
-      TileWalk w{tile_off, p.batch, 0, 0};
-      w.start(u0);
+      int b = 0, j = 0;
+      locate(tile_off, p.batch, u0, b, j);
       int cur_b = -1, L = 0;
       float wt[kHeads];
       int64_t n = 0;
-      for (int64_t u = u0; u < u1; ++u, ++n, w.next()) {
-        if (w.b != cur_b) {
-          cur_b = w.b;
+      // Adds this warp's histogram of request `fb` into the global one.
+      auto flush = [&](int fb) {
+        __syncwarp();
+        for (int i = lane; i < kBins; i += 32) {
+          const uint32_t v = hist[i];
+          if (v) { atomicAdd(p.hist + static_cast<int64_t>(fb) * kBins + i, v); hist[i] = 0; }
+        }
+        __syncwarp();
+      };
+      for (int64_t u = u0; u < u1; ++u, ++n) {
+        if (b != cur_b) {
+          if (cur_b >= 0) flush(cur_b);
+          cur_b = b;
           L = clamp_len(__ldg(p.seq_lens + cur_b), max_len, p.status);
 #pragma unroll
           for (int h = 0; h < kHeads; ++h) wt[h] = __ldg(p.weights + cur_b * kHeads + h);
         }
-        const int tok = w.j * kTileTok + row;
+        const int tok = j * kTileTok + row;
         const bool valid = tok < L;
-        float scale = 0.f;
-        if (valid) {
-          const int pid = page_id(p, cur_b, tok >> 6);
-          scale = __ldg(reinterpret_cast<const float*>(
-              p.k_cache + static_cast<int64_t>(pid) * kPageBytes + kPageDataBytes + (tok & 63) * 4));
-        }
+        const int s = static_cast<int>(n % kStages);
         const int a = static_cast<int>(n % kAccStages);
         const uint32_t aph = static_cast<uint32_t>((n / kAccStages) & 1);
-        if (!mbar_wait(&accfull[a], aph, wctx)) break;
+        // accfull implies the stage's data landed; waiting on the stage's own
+        // barrier too makes the bulk-copied scales visible to this thread.
+        // (The stage cannot be refilled before this warp arrives on empty[s].)
+        bool good = mbar_wait(&accfull[a], aph, wctx);
+        good = good && mbar_wait(&full[s], static_cast<uint32_t>((n / kStages) & 1), wctx);
+        if (!__all_sync(0xffffffffu, good)) break;
         tc_fence_after();
+        const float scale = *reinterpret_cast<const float*>(
+            stage_mem + s * kStageStride + kStageData + (row >> 6) * kScaleBytes + (row & 63) * 4);
         float acc[kHeads];
         {
           float lo[32], hi[32];
@@ -307,7 +374,8 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
           for (int h = 0; h < 32; ++h) { acc[h] = lo[h]; acc[h + 32] = hi[h]; }
         }
         tc_fence_before();
-        mbar_arrive(&accempty[a]);
+        __syncwarp();
+        if (lane == 0) { mbar_arrive(&accempty[a]); mbar_arrive(&empty[s]); }
         if (valid) {
           // relu(v) written as the reference does: v <= 0 ? 0 : v (NaN passes).
           float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
@@ -320,9 +388,16 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
             s2 += (x2 <= 0.f ? 0.f : x2) * wt[h + 2];
             s3 += (x3 <= 0.f ? 0.f : x3) * wt[h + 3];
           }
-          p.scores[static_cast<int64_t>(cur_b) * p.score_stride + tok] = (s0 + s1) + (s2 + s3);
+          const float sc = (s0 + s1) + (s2 + s3);
+          p.scores[static_cast<int64_t>(cur_b) * p.score_stride + tok] = sc;
+          atomicAdd(&hist[score_key(sc) >> 21], 1u);
+        }
+        if (++j == tile_off[b + 1] - tile_off[b]) {
+          j = 0;
+          do { ++b; } while (b < p.batch && tile_off[b + 1] == tile_off[b]);
         }
       }
+      if (cur_b >= 0) flush(cur_b);
     }
   }
 
@@ -337,12 +412,12 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
 // ------------------------------------------------------------ top-k select
 constexpr int kSelThreads = 1024;
 constexpr int kTopK = DSA_TOPK;
-constexpr int kBins = 2048;
 constexpr int kCandCap = 16384;
 constexpr size_t kSelSmem = sizeof(uint64_t) * (kTopK + kCandCap) + sizeof(uint32_t) * kBins + 256;
 
 struct SelectParams {
   const float* scores;
+  unsigned int* hist;
   const int32_t* seq_lens;
   const int32_t* block_table;
   int32_t* out;
@@ -380,7 +455,7 @@ __device__ __forceinline__ int block_scan_incl(int v, int* warp_tot) {
 }
 
 // Finds the bin d (scanning from the highest bin down) that holds the
-// need-th largest element; returns d, the count strictly above d and hist[d].
+// need-th largest element; res = {d, count strictly above d, hist[d]}.
 __device__ __forceinline__ void find_bin(const uint32_t* hist, int need, int* warp_tot, int* res) {
   const int t = threadIdx.x;
   const int hi = kBins - 1 - 2 * t, lo = hi - 1;
@@ -390,6 +465,69 @@ __device__ __forceinline__ void find_bin(const uint32_t* hist, int need, int* wa
   if (excl < need && need <= excl + a) { res[0] = hi; res[1] = excl; res[2] = a; }
   else if (excl + a < need && need <= incl) { res[0] = lo; res[1] = excl + a; res[2] = c; }
   __syncthreads();
+}
+
+// Appends v to buf when pred holds; one shared atomic per warp.
+__device__ __forceinline__ void warp_append(bool pred, uint64_t v, uint64_t* buf, int* counter,
+                                            int cap) {
+  const unsigned m = __ballot_sync(0xffffffffu, pred);
+  if (m == 0) return;
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(m) - 1;
+  int base = 0;
+  if (lane == leader) base = atomicAdd(counter, __popc(m));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  const int pos = base + __popc(m & ((1u << lane) - 1u));
+  if (pred && pos < cap) buf[pos] = v;
+}
+
+// 64-bit compare-exchange steps of a descending bitonic sort whose partner
+// lives in another lane of the same warp (distance j in 2..32 elements, two
+// elements per thread at 2t and 2t+1).
+__device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int m) {
+  const uint32_t lo = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v), m);
+  const uint32_t hi = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), m);
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
+__device__ __forceinline__ void reg_steps(uint64_t& x0, uint64_t& x1, int k, int jmax) {
+  const int t = threadIdx.x;
+  for (int j = jmax; j >= 1; j >>= 1) {
+    if (j == 1) {
+      const bool desc = ((2 * t) & k) == 0;
+      if (desc ? (x0 < x1) : (x0 > x1)) { const uint64_t tmp = x0; x0 = x1; x1 = tmp; }
+    } else {
+      const uint64_t y0 = shfl_xor64(x0, j >> 1), y1 = shfl_xor64(x1, j >> 1);
+      const int i0 = 2 * t;
+      const bool lo_side = (i0 & j) == 0;
+      const bool desc = (i0 & k) == 0;
+      const bool keep_max = lo_side == desc;
+      x0 = keep_max ? (x0 > y0 ? x0 : y0) : (x0 < y0 ? x0 : y0);
+      x1 = keep_max ? (x1 > y1 ? x1 : y1) : (x1 < y1 ? x1 : y1);
+    }
+  }
+}
+
+__device__ void bitonic_sort_desc_2048(uint64_t* sel) {
+  const int t = threadIdx.x;
+  uint64_t x0 = sel[2 * t], x1 = sel[2 * t + 1];
+  for (int k = 2; k <= 64; k <<= 1) reg_steps(x0, x1, k, k >> 1);
+  sel[2 * t] = x0; sel[2 * t + 1] = x1;
+  __syncthreads();
+  for (int k = 128; k <= kTopK; k <<= 1) {
+    for (int j = k >> 1; j >= 64; j >>= 1) {
+      const int lo = 2 * j * (t / j) + (t % j);
+      const int hi = lo + j;
+      const uint64_t a = sel[lo], b = sel[hi];
+      const bool desc = (lo & k) == 0;
+      if (desc ? (a < b) : (a > b)) { sel[lo] = b; sel[hi] = a; }
+      __syncthreads();
+    }
+    x0 = sel[2 * t]; x1 = sel[2 * t + 1];
+    reg_steps(x0, x1, k, 32);
+    sel[2 * t] = x0; sel[2 * t + 1] = x1;
+    __syncthreads();
+  }
 }
 
 __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const SelectParams p) {
@@ -403,36 +541,36 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
 
   const int b = blockIdx.x;
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
   const int max_len = p.max_pages * kPage;
   int L = __ldg(p.seq_lens + b);
   L = L < 0 ? 0 : (L > max_len ? max_len : L);  // the score kernel flags bad lengths
   const float* row = p.scores + static_cast<int64_t>(b) * p.score_stride;
+  unsigned int* ghist = p.hist + static_cast<int64_t>(b) * kBins;
   const int K = L < kTopK ? L : kTopK;
+
+  // Take the histogram the score kernel accumulated, and leave zeros behind.
+  for (int i = tid; i < kBins; i += kSelThreads) { hist[i] = ghist[i]; ghist[i] = 0; }
+  if (tid == 0) { counters[0] = 0; counters[1] = 0; }
+  __syncthreads();
 
   if (L <= kTopK) {
     for (int i = tid; i < kTopK; i += kSelThreads) sel[i] = i < L ? composite(row[i], i) : 0ull;
     __syncthreads();
   } else {
-    // Pass 1: histogram of the top 11 key bits over all L scores.
-    for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
-    if (tid == 0) { counters[0] = 0; counters[1] = 0; }
-    __syncthreads();
-    for (int i = tid; i < L; i += kSelThreads) atomicAdd(&hist[score_key(row[i]) >> 21], 1u);
-    __syncthreads();
     find_bin(hist, K, warp_tot, res);
     const uint32_t bin1 = static_cast<uint32_t>(res[0]);
     int need = K - res[1];
     int count = res[2];
-    // Pass 2: higher bins are winners; the boundary bin becomes candidates.
-    for (int i = tid; i < L; i += kSelThreads) {
-      const float s = row[i];
+    // One pass: higher bins are winners; the boundary bin becomes candidates.
+    const int Lr = (L + 31) & ~31;
+    for (int i = tid; i < Lr; i += kSelThreads) {
+      const bool in = i < L;
+      const float s = in ? row[i] : 0.f;
       const uint32_t d = score_key(s) >> 21;
-      if (d > bin1) {
-        sel[atomicAdd(&counters[0], 1)] = composite(s, i);
-      } else if (d == bin1) {
-        const int c = atomicAdd(&counters[1], 1);
-        if (c < kCandCap) cand[c] = composite(s, i);
-      }
+      const uint64_t c = composite(s, i);
+      warp_append(in && d > bin1, c, sel, &counters[0], kTopK);
+      warp_append(in && d == bin1, c, cand, &counters[1], kCandCap);
     }
     __syncthreads();
     const int ncand = counters[1];
@@ -467,30 +605,23 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     }
     // Collect the boundary-bin winners: (c & mask) >= prefix.
     if (in_smem) {
-      for (int i = tid; i < ncand; i += kSelThreads) {
-        const uint64_t c = cand[i];
-        if ((c & mask) >= prefix) sel[atomicAdd(&counters[0], 1)] = c;
+      const int nr = (ncand + 31) & ~31;
+      for (int i = tid; i < nr; i += kSelThreads) {
+        const uint64_t c = i < ncand ? cand[i] : 0ull;
+        warp_append(i < ncand && (c & mask) >= prefix, c, sel, &counters[0], kTopK);
       }
     } else {
-      for (int i = tid; i < L; i += kSelThreads) {
-        const uint64_t c = composite(row[i], i);
-        if ((c >> 53) == bin1 && (c & mask) >= prefix) sel[atomicAdd(&counters[0], 1)] = c;
+      for (int i = tid; i < Lr; i += kSelThreads) {
+        const bool in = i < L;
+        const uint64_t c = in ? composite(row[i], i) : 0ull;
+        warp_append(in && (c >> 53) == bin1 && (c & mask) >= prefix, c, sel, &counters[0], kTopK);
       }
     }
     __syncthreads();
   }
+  (void)lane;
 
-  // Bitonic sort of the 2048 composite keys, descending.
-  for (int k = 2; k <= kTopK; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      const int lo = 2 * j * (tid / j) + (tid % j);
-      const int hi = lo + j;
-      const uint64_t x = sel[lo], y = sel[hi];
-      const bool desc = (lo & k) == 0;
-      if (desc ? (x < y) : (x > y)) { sel[lo] = y; sel[hi] = x; }
-      __syncthreads();
-    }
-  }
+  bitonic_sort_desc_2048(sel);
 
   int32_t* out = p.out + static_cast<int64_t>(b) * kTopK;
   const int32_t* bt = p.block_table + static_cast<int64_t>(b) * p.max_pages;
@@ -514,7 +645,7 @@ using namespace dsa;
 
 extern "C" size_t dsa_indexer_workspace_bytes(int32_t batch, int32_t max_pages) {
   if (batch < 0 || max_pages < 0) return 0;
-  return kWorkspaceHeader +
+  return kWorkspaceHeader + sizeof(uint32_t) * static_cast<size_t>(batch) * ix::kBins +
          sizeof(float) * static_cast<size_t>(batch) * static_cast<size_t>(max_pages) * ix::kPage;
 }
 
@@ -569,7 +700,10 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
   sp.weights = weights;
   sp.seq_lens = seq_lens;
   sp.block_table = block_table;
-  sp.scores = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeader);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  sp.hist = reinterpret_cast<unsigned int*>(ws + kWorkspaceHeader);
+  sp.scores = reinterpret_cast<float*>(ws + kWorkspaceHeader +
+                                       sizeof(uint32_t) * static_cast<size_t>(batch) * ix::kBins);
   sp.status = static_cast<unsigned int*>(workspace);
   sp.num_pages = num_pages;
   sp.batch = batch;
@@ -579,6 +713,7 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
 
   ix::SelectParams selp;
   selp.scores = sp.scores;
+  selp.hist = sp.hist;
   selp.seq_lens = seq_lens;
   selp.block_table = block_table;
   selp.out = topk_indices;

@@ -81,7 +81,11 @@ DSA_API int dsa_b200_abi_version(void);
 DSA_API const char* dsa_b200_status_string(int status);
 
 /* Bytes of device workspace dsa_indexer_run needs for this batch and block
- * table width (256-byte header + fp32 score rows). */
+ * table width: a 256-byte header, a [batch, 2048] uint32 radix histogram and
+ * [batch, max_pages*64] fp32 score rows.  The workspace must be zero-filled
+ * before its first use; every completed call leaves the histogram region
+ * zero again, so it can be reused without clearing (re-zero it after a call
+ * that raised DSA_DEV_WAIT_TIMEOUT). */
 DSA_API size_t dsa_indexer_workspace_bytes(int32_t batch, int32_t max_pages);
 
 /* FP8 lightning indexer, decode (one query token per request).

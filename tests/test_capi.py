@@ -40,7 +40,7 @@ def test_version_and_status_strings():
 
 def test_workspace_sizes():
     lib = _native.lib()
-    assert lib.dsa_indexer_workspace_bytes(64, 1024) == 256 + 4 * 64 * 1024 * 64
+    assert lib.dsa_indexer_workspace_bytes(64, 1024) == 256 + 4 * 64 * 2048 + 4 * 64 * 1024 * 64
     assert lib.dsa_indexer_workspace_bytes(0, 10) == 256
     assert lib.dsa_attention_workspace_bytes(0) == 256
     assert lib.dsa_attention_workspace_bytes(8) > lib.dsa_attention_workspace_bytes(1)
@@ -56,7 +56,7 @@ FAKE = ctypes.c_void_p(4096)  # never dereferenced: every case fails validation 
     (4, 1, 1, NULL, 1),         # null pointers
     (4, 0, 1, FAKE, 1),         # max_pages < 1
     (4, 1, 0, FAKE, 1),         # empty pool
-    (9000, 1, 1, FAKE, 1),      # batch above the per-call limit
+    (5000, 1, 1, FAKE, 1),      # batch above the per-call limit
 ])
 def test_indexer_host_validation(batch, max_pages, num_pages, ptr, expect):
     lib = _native.lib()
