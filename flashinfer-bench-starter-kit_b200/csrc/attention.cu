@@ -21,7 +21,9 @@
 //                issuing logits and PV in whatever order their inputs
 //                become ready:
 //                  S^T[64 rows, 16 heads]  = K[64, 576] . Q[16, 576]^T
-//                  (M = 64, N = 16, 36 x K16), then after the softmax
+//                  (M = 64, N = 16, 36 x K16 spread over 4 independent
+//                  partial accumulators, so consecutive MMAs never wait on
+//                  each other's result), then after the softmax
 //                  O^T[512, 16] += V^T[512, 64] . P^T[64, 16]
 //                  (4 x M = 128, N = 16, 4 x K16); V^T is the same shared
 //                  memory as the ckv chunks, read MN-major.
@@ -29,10 +31,10 @@
 //                max is only moved when a tile exceeds it by more than 8,
 //                so O in TMEM is rarely touched), P^T written as bf16.
 //   A token fully covered by one CTA is normalised and written directly;
-//   otherwise the CTA writes (O, m, l) partials.
-//
-//   attention_combine_kernel merges the partials of split tokens:
-//   lse = log2 sum_i l_i 2^(m_i - M) + M, out = sum_i O_i 2^(m_i - M) / l.
+//   otherwise each covering CTA writes an (O, m, l) partial and bumps a
+//   per-token counter; the last one to arrive merges them:
+//   lse = log2 sum_i l_i 2^(m_i - M) + M, out = sum_i O_i 2^(m_i - M) / l,
+//   and resets the counter (so the workspace stays ready for the next call).
 #include <cuda_bf16.h>
 
 #include <cmath>
@@ -62,7 +64,7 @@ constexpr int kSoftWarp0 = 5;                    // warps 5-8: online softmax
 constexpr int kThreads = 288;
 constexpr int kTmemCols = 256;
 constexpr uint32_t kColO = 0;    // O^T buffers at [0,64) and [64,128): 4 blocks x 16 heads
-constexpr uint32_t kColS = 128;  // S^T buffers at [128,144) and [144,160)
+constexpr uint32_t kColS = 128;  // S^T buffers at [128,192) and [192,256): 4 partial sums x 16 heads
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: factor 256
 constexpr int kMaxTokens = (1 << 30) / (kTopK / kRows) / kHeads;
 
@@ -86,6 +88,7 @@ struct Params {
   float* lse;
   float* part_o;   // [records][16][512]
   float* part_ml;  // [records][16][2]
+  int* tok_count;  // [num_tokens] partials written so far, zero between calls
   unsigned int* status;
   int64_t num_slots;
   int num_tokens;
@@ -96,6 +99,84 @@ struct Params {
 // Which tokens / records a CTA covers, shared by both kernels.
 __host__ __device__ inline int64_t unit_start(int64_t total, int c, int grid) {
   return total * c / grid;
+}
+
+// CTAs c whose unit range [start(c), start(c+1)) meets token t's units.
+__device__ __forceinline__ void covering_ctas(int t, int64_t total, int grid, int& c_lo, int& c_hi) {
+  const int64_t a = static_cast<int64_t>(t) * kTilesPerTok, z = a + kTilesPerTok;
+  int c = static_cast<int>(a * grid / total);
+  while (c > 0 && unit_start(total, c, grid) > a) --c;
+  while (unit_start(total, c + 1, grid) <= a) ++c;
+  c_lo = c;
+  while (c + 1 < grid && unit_start(total, c + 1, grid) < z) ++c;
+  c_hi = c;
+}
+
+__device__ __forceinline__ int parts_of(int t, int64_t total, int grid) {
+  int lo, hi;
+  covering_ctas(t, total, grid, lo, hi);
+  return hi - lo + 1;
+}
+
+// Merges the (O, m, l) partials of token t; run by the 128 softmax threads of
+// the CTA that wrote the last partial.  scratch: >= 16 * 33 floats of smem.
+__device__ void merge_token(const Params& p, int t, int64_t total, int grid, int e, float* scratch) {
+  int c_lo, c_hi;
+  covering_ctas(t, total, grid, c_lo, c_hi);
+  const int nparts = c_hi - c_lo + 1;
+  // Per-head weights w[i][h] = 2^(m_i - M) / l, and lse.
+  if (e < kHeads) {
+    float M = -INFINITY;
+    for (int c = c_lo; c <= c_hi; ++c) {
+      const int64_t rec = static_cast<int64_t>(c) * p.kmax +
+                          (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
+      M = fmaxf(M, __ldcg(p.part_ml + rec * 2 * kHeads + 2 * e));
+    }
+    float l = 0.f;
+    for (int c = c_lo; c <= c_hi; ++c) {
+      const int64_t rec = static_cast<int64_t>(c) * p.kmax +
+                          (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
+      const float mi = __ldcg(p.part_ml + rec * 2 * kHeads + 2 * e);
+      const float li = __ldcg(p.part_ml + rec * 2 * kHeads + 2 * e + 1);
+      const float w = mi == -INFINITY ? 0.f : exp2f(mi - M);
+      scratch[(c - c_lo) * kHeads + e] = w;
+      l += li * w;
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    for (int i = 0; i < nparts; ++i) scratch[i * kHeads + e] *= inv;
+    p.lse[static_cast<int64_t>(t) * kHeads + e] = l > 0.f ? M + log2f(l) : -INFINITY;
+  }
+  named_barrier_sync(1, 128);
+  // Thread e combines 64 consecutive outputs: head e/8, columns 64*(e%8)...
+  const int h = e >> 3;
+  const int c0 = (e & 7) * 64;
+  float acc[64];
+#pragma unroll
+  for (int k = 0; k < 64; ++k) acc[k] = 0.f;
+  for (int c = c_lo; c <= c_hi; ++c) {
+    const int64_t rec = static_cast<int64_t>(c) * p.kmax +
+                        (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
+    const float w = scratch[(c - c_lo) * kHeads + h];
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + (rec * kHeads + h) * kCkv + c0);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float4 v = __ldcg(src + k);
+      acc[4 * k] += v.x * w; acc[4 * k + 1] += v.y * w;
+      acc[4 * k + 2] += v.z * w; acc[4 * k + 3] += v.w * w;
+    }
+  }
+  __nv_bfloat16* out = p.out + (static_cast<int64_t>(t) * kHeads + h) * kCkv + c0;
+#pragma unroll
+  for (int k = 0; k < 64; k += 8) {
+    __nv_bfloat162 a0 = __floats2bfloat162_rn(acc[k], acc[k + 1]);
+    __nv_bfloat162 a1 = __floats2bfloat162_rn(acc[k + 2], acc[k + 3]);
+    __nv_bfloat162 a2 = __floats2bfloat162_rn(acc[k + 4], acc[k + 5]);
+    __nv_bfloat162 a3 = __floats2bfloat162_rn(acc[k + 6], acc[k + 7]);
+    uint4 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&a0); pk.y = *reinterpret_cast<uint32_t*>(&a1);
+    pk.z = *reinterpret_cast<uint32_t*>(&a2); pk.w = *reinterpret_cast<uint32_t*>(&a3);
+    *reinterpret_cast<uint4*>(out + k) = pk;
+  }
 }
 
 __device__ __forceinline__ int sanitize_slot(int v, int64_t num_slots, unsigned int* status) {
@@ -269,12 +350,13 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             tc_fence_after();
             const uint64_t ad = st_desc0 + s * (kStageBytes >> 4);
             const uint64_t bd = q_desc0 + (seg & 1) * (kQBytes >> 4);
-            const uint32_t d = tmem_base + kColS + 16u * s;
+            const uint32_t d = tmem_base + kColS + 64u * s;
 #pragma unroll
             for (int k = 0; k < kChunks * 4; ++k) {
-              // +8192 bytes per 64-column chunk, +32 bytes per K16 step (>> 4)
-              umma_bf16(d, ad + (k >> 2) * (kChunkBytes >> 4) + (k & 3) * 2,
-                        bd + (k >> 2) * (kQChunkBytes >> 4) + (k & 3) * 2, kIdescS, k > 0 ? 1u : 0u);
+              // K16 step k -> partial accumulator k % 4.  Descriptor offsets:
+              // +8192 bytes per 64-column chunk, +32 bytes per K16 step (>> 4).
+              umma_bf16(d + 16 * (k & 3), ad + (k >> 2) * (kChunkBytes >> 4) + (k & 3) * 2,
+                        bd + (k >> 2) * (kQChunkBytes >> 4) + (k & 3) * 2, kIdescS, k >= 4 ? 1u : 0u);
             }
             umma_commit(&s_full[s]);
             if (seg_end) umma_commit(&q_empty[seg & 1]);
@@ -293,9 +375,9 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             tc_fence_after();
             const uint32_t obuf = tmem_base + kColO + 64u * (seg & 1);
 #pragma unroll
-            for (int mb = 0; mb < 4; ++mb) {
+            for (int kk = 0; kk < kRows / 16; ++kk) {
 #pragma unroll
-              for (int kk = 0; kk < kRows / 16; ++kk) {
+              for (int mb = 0; mb < 4; ++mb) {
                 // V^T block mb: chunks 2mb, 2mb+1; K16 step = 16 rows = 2048 bytes
                 umma_bf16(obuf + 16 * mb,
                           v_desc0 + s * (kStageBytes >> 4) + mb * (2 * kChunkBytes >> 4) + kk * (2048 >> 4),
@@ -352,8 +434,14 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
       bool ok = mbar_wait(&s_full[s], (i >> 1) & 1, wctx);
       tc_fence_after();
       float sv[16];
-      tmem_ld16(tmem_base + lane_base + kColS + 16u * s, sv);
-      tmem_wait_ld();
+      {
+        float lo[32], hi[32];
+        tmem_ld32(tmem_base + lane_base + kColS + 64u * s, lo);
+        tmem_ld32(tmem_base + lane_base + kColS + 64u * s + 32, hi);
+        tmem_wait_ld();
+#pragma unroll
+        for (int hh = 0; hh < kHeads; ++hh) sv[hh] = (lo[hh] + lo[16 + hh]) + (hi[hh] + hi[16 + hh]);
+      }
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
       if (lane < 16) {
@@ -481,8 +569,25 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             p.part_ml[rec * 2 * kHeads + 2 * e] = ml_smem[2 * e];
             p.part_ml[rec * 2 * kHeads + 2 * e + 1] = ml_smem[2 * e + 1];
           }
+          // Publish the partial, count it, and let the last CTA merge.
+          __threadfence();
+          named_barrier_sync(1, 128);
+          if (e == 0) {
+            const int prev = atomicAdd(p.tok_count + t, 1);
+            const int last = prev == parts_of(t, total, gridDim.x) - 1;
+            if (last) p.tok_count[t] = 0;
+            *rescale_flag = last ? 2 : 0;  // reuse the flag word as a broadcast
+          }
+          named_barrier_sync(1, 128);
+          const bool last = *rescale_flag == 2;
+          named_barrier_sync(1, 128);
+          if (e == 0) *rescale_flag = 0;
+          if (last) {
+            __threadfence();
+            merge_token(p, t, total, gridDim.x, e, sx);
+          }
         }
-        named_barrier_sync(1, 128);  // ml_smem is rewritten by the next segment
+        named_barrier_sync(1, 128);  // ml_smem / sx are rewritten by the next segment
       }
     }
   }
@@ -493,56 +598,6 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
-}
-
-// One CTA per token; does nothing for tokens a single CTA finished.
-__global__ void __launch_bounds__(256) attention_combine_kernel(const Params p, int grid) {
-  const int t = blockIdx.x;
-  const int64_t total = static_cast<int64_t>(p.num_tokens) * kTilesPerTok;
-  const int64_t a = static_cast<int64_t>(t) * kTilesPerTok, z = a + kTilesPerTok;
-  int c = static_cast<int>(a * grid / total);
-  while (c > 0 && unit_start(total, c, grid) > a) --c;
-  while (unit_start(total, c + 1, grid) <= a) ++c;
-  if (unit_start(total, c, grid) <= a && unit_start(total, c + 1, grid) >= z) return;
-
-  const int tid = threadIdx.x;
-  const int h = tid >> 4;            // 16 threads per head
-  const int c0 = (tid & 15) * 32;    // 32 columns each
-  float M = -INFINITY;
-  for (int cc = c; cc < grid && unit_start(total, cc, grid) < z; ++cc) {
-    const int64_t rec = static_cast<int64_t>(cc) * p.kmax +
-                        (t - static_cast<int>(unit_start(total, cc, grid) / kTilesPerTok));
-    M = fmaxf(M, p.part_ml[rec * 2 * kHeads + 2 * h]);
-  }
-  float l = 0.f;
-  float acc[32];
-#pragma unroll
-  for (int k = 0; k < 32; ++k) acc[k] = 0.f;
-  if (M != -INFINITY) {
-    for (int cc = c; cc < grid && unit_start(total, cc, grid) < z; ++cc) {
-      const int64_t rec = static_cast<int64_t>(cc) * p.kmax +
-                          (t - static_cast<int>(unit_start(total, cc, grid) / kTilesPerTok));
-      const float mi = p.part_ml[rec * 2 * kHeads + 2 * h];
-      const float li = p.part_ml[rec * 2 * kHeads + 2 * h + 1];
-      if (mi == -INFINITY) continue;
-      const float wgt = exp2f(mi - M);
-      l += li * wgt;
-      const float4* src = reinterpret_cast<const float4*>(p.part_o + (rec * kHeads + h) * kCkv + c0);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float4 v = src[k];
-        acc[4 * k] += v.x * wgt; acc[4 * k + 1] += v.y * wgt;
-        acc[4 * k + 2] += v.z * wgt; acc[4 * k + 3] += v.w * wgt;
-      }
-    }
-  }
-  const float inv = l > 0.f ? 1.f / l : 0.f;
-  __nv_bfloat16* out = p.out + (static_cast<int64_t>(t) * kHeads + h) * kCkv + c0;
-#pragma unroll
-  for (int k = 0; k < 32; k += 2)
-    *reinterpret_cast<__nv_bfloat162*>(out + k) = __floats2bfloat162_rn(acc[k] * inv, acc[k + 1] * inv);
-  if ((tid & 15) == 0)
-    p.lse[static_cast<int64_t>(t) * kHeads + h] = l > 0.f ? M + log2f(l) : -INFINITY;
 }
 
 inline int grid_for(int num_tokens, int num_sms) {
@@ -560,7 +615,8 @@ inline size_t workspace_for(int num_tokens, int num_sms) {
   if (num_tokens <= 0) return kWorkspaceHeader;
   const int grid = grid_for(num_tokens, num_sms);
   const size_t recs = static_cast<size_t>(grid) * kmax_for(num_tokens, grid);
-  return kWorkspaceHeader + recs * kHeads * (kCkv + 2) * sizeof(float);
+  return kWorkspaceHeader + recs * kHeads * (kCkv + 2) * sizeof(float) +
+         sizeof(int) * static_cast<size_t>(num_tokens);
 }
 
 std::once_flag g_attr_once[64];
@@ -635,6 +691,7 @@ extern "C" int dsa_attention_run(const void* q_nope, const void* q_pe, const voi
   prm.lse = lse;
   prm.part_o = reinterpret_cast<float*>(ws + kWorkspaceHeader);
   prm.part_ml = prm.part_o + recs * attn::kHeads * attn::kCkv;
+  prm.tok_count = reinterpret_cast<int*>(prm.part_ml + recs * attn::kHeads * 2);
   prm.status = reinterpret_cast<unsigned int*>(ws);
   prm.num_slots = num_slots;
   prm.num_tokens = num_tokens;
@@ -644,7 +701,6 @@ extern "C" int dsa_attention_run(const void* q_nope, const void* q_pe, const voi
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   attn::attention_kernel<<<grid, attn::kThreads, attn::kSmemBytes, s>>>(ckv_map, kpe_map, qn_map,
                                                                        qp_map, prm);
-  attn::attention_combine_kernel<<<num_tokens, 256, 0, s>>>(prm, grid);
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
   return DSA_OK;
 }

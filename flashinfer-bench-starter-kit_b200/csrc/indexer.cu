@@ -7,13 +7,13 @@
 //    concatenation over requests of 128-token tiles (two 64-token pages);
 //    CTA c takes the contiguous slice [c*U/G, (c+1)*U/G) of the U tiles, so
 //    load balance does not depend on how seq_lens are distributed.  Roles:
-//      warp 0      TMA producer: raw FP8 pages (64 rows x 128 B, 128-byte
-//                  swizzle) plus each page's 64 fp32 scales (bulk copy)
-//                  straight from the paged cache into an 8-deep shared-memory
-//                  ring, and q[b] (64 heads x 128 B) when the request changes.
-//                  The warp resolves the block-table entries of 32 tiles at a
-//                  time, one group ahead, so no load latency sits between
-//                  two TMA issues.  Nothing is dequantised in HBM
+//      warps 0,6   TMA producers: raw FP8 pages (64 rows x 128 B, 128-byte
+//                  swizzle; warp 0) and each page's 64 fp32 scales (bulk
+//                  copy; warp 6) straight from the paged cache into an
+//                  8-deep shared-memory ring, and q[b] (64 heads x 128 B)
+//                  when the request changes.  Block-table entries are
+//                  resolved 32 tiles at a time, one group ahead, so no load
+//                  latency sits between two copy issues.  Nothing is dequantised in HBM
 //                  (the reference writes an fp32 copy of K, kernel.py:108-135).
 //      warp 1      MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 tokens,
 //                  N = 64 heads, K = 128 (4 x K32), fp32 accumulator in TMEM,
@@ -58,7 +58,8 @@ constexpr int kStageStride = kStageData + 1024;           // + the two pages' sc
 constexpr int kStages = 8;
 constexpr int kAccStages = 4;
 constexpr int kTmemCols = kAccStages * kHeads;            // 256
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;                            // 7 warps
+constexpr int kScaleWarp = 6;                           // second producer: scale copies
 constexpr int kEpiWarps = 4;
 constexpr int kBins = 2048;                               // radix bins: top 11 key bits
 constexpr int kMaxBatch = 4096;
@@ -74,7 +75,8 @@ constexpr int kOffHist = kOffQ + 2 * kPageDataBytes;              // 155648
 constexpr int kOffBar = kOffHist + kEpiWarps * kBins * 4;         // 188416
 constexpr int kNumBars = 2 * kStages + 4 + 2 * kAccStages + 1;
 constexpr int kOffMisc = kOffBar + 256;
-constexpr int kOffTiles = kOffMisc + 64;
+constexpr int kOffInfo = kOffMisc + 64;                           // 2 producer warps x 32 tiles
+constexpr int kOffTiles = kOffInfo + 2 * 32 * 5 * 4;
 static_assert(kNumBars * 8 <= 256, "barrier area");
 
 inline size_t score_smem_bytes(int batch) {
@@ -181,7 +183,8 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   if (tid == 0) {
     // A stage is free again once its MMAs completed (1 commit) and every
     // epilogue warp has read the stage's token scales (4 arrivals).
-    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + kEpiWarps); }
+    // full: one arrive.expect_tx from each producer warp (data, scales).
+    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 2); mbar_init(&empty[s], 1 + kEpiWarps); }
     for (int s = 0; s < 2; ++s) { mbar_init(&qfull[s], 1); mbar_init(&qempty[s], 1); }
     for (int s = 0; s < kAccStages; ++s) { mbar_init(&accfull[s], 1); mbar_init(&accempty[s], kEpiWarps); }
     mbar_init(drain, 1);
@@ -232,53 +235,58 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   const int64_t u1 = total * (blockIdx.x + 1) / gridDim.x;
   const WaitCtx wctx{abort_flag, p.status};
 
-  if (warp == 0) {
-    // ------------------------------------------------------ TMA producer warp
+  if (warp == 0 || warp == kScaleWarp) {
+    // ------------------------------------------------------ producer warps
+    // Warp 0 issues the two FP8 page boxes of each tile (and q[b] when the
+    // request changes); warp 6 issues the two 256-byte scale copies.  A
+    // thread issues TMA / bulk copies at a fixed rate, so splitting the four
+    // copies of a tile over two warps halves the issue time per tile.  Each
+    // warp resolves the block-table entries of 32 tiles at once, one group
+    // ahead, and stages them in shared memory for its issuing lane.
+    const bool data_warp = warp == 0;
+    TileInfo* info = reinterpret_cast<TileInfo*>(smem + kOffInfo) + (data_warp ? 0 : 32);
     const uint64_t policy = make_policy_evict_first();
     int cur_b = -1, nq = 0;
     int64_t n = 0;
-    bool ok = true;
+    int ok = 1;
     TileInfo nxt = tile_info(p, tile_off, u0 + lane, u1, max_len);
     for (int64_t g0 = u0; g0 < u1 && ok; g0 += 32) {
-      const TileInfo cur = nxt;
+      info[lane] = nxt;
       nxt = tile_info(p, tile_off, g0 + 32 + lane, u1, max_len);  // one group ahead
+      __syncwarp();
       const int cnt = static_cast<int>(u1 - g0 < 32 ? u1 - g0 : 32);
-      for (int t = 0; t < cnt; ++t, ++n) {
-        const int b = __shfl_sync(0xffffffffu, cur.b, t);
-        const int npg = __shfl_sync(0xffffffffu, cur.npg, t);
-        const int p0 = __shfl_sync(0xffffffffu, cur.p0, t);
-        const int p1 = __shfl_sync(0xffffffffu, cur.p1, t);
-        int good = 1;
-        if (lane == 0) {
-          if (b != cur_b) {
+      if (lane == 0) {
+        for (int t = 0; t < cnt; ++t, ++n) {
+          const TileInfo ti = info[t];
+          if (data_warp && ti.b != cur_b) {
             const int slot = nq & 1;
-            good = mbar_wait(&qempty[slot], ((nq >> 1) & 1) ^ 1, wctx);
-            if (good) {
-              mbar_arrive_expect_tx(&qfull[slot], kPageDataBytes);
-              tma_load_2d(q_mem + slot * kPageDataBytes, &qmap, &qfull[slot], 0, b * kHeads);
-            }
+            if (!mbar_wait(&qempty[slot], ((nq >> 1) & 1) ^ 1, wctx)) { ok = 0; break; }
+            mbar_arrive_expect_tx(&qfull[slot], kPageDataBytes);
+            tma_load_2d(q_mem + slot * kPageDataBytes, &qmap, &qfull[slot], 0, ti.b * kHeads);
             ++nq;
           }
+          cur_b = ti.b;
           const int s = static_cast<int>(n % kStages);
-          const uint32_t ph = static_cast<uint32_t>((n / kStages) & 1);
-          good = good && mbar_wait(&empty[s], ph ^ 1, wctx);
-          if (good) {
-            uint8_t* st = stage_mem + s * kStageStride;
-            mbar_arrive_expect_tx(&full[s], npg * (kPageDataBytes + kScaleBytes));
-            tma_load_2d_hint(st, &kmap, &full[s], 0, p0 * kPageRows, policy);
-            bulk_load(st + kStageData, p.k_cache + static_cast<int64_t>(p0) * kPageBytes + kPageDataBytes,
+          if (!mbar_wait(&empty[s], static_cast<uint32_t>(((n / kStages) & 1) ^ 1), wctx)) { ok = 0; break; }
+          uint8_t* st = stage_mem + s * kStageStride;
+          if (data_warp) {
+            mbar_arrive_expect_tx(&full[s], ti.npg * kPageDataBytes);
+            tma_load_2d_hint(st, &kmap, &full[s], 0, ti.p0 * kPageRows, policy);
+            if (ti.npg == 2)
+              tma_load_2d_hint(st + kPageDataBytes, &kmap, &full[s], 0, ti.p1 * kPageRows, policy);
+          } else {
+            mbar_arrive_expect_tx(&full[s], ti.npg * kScaleBytes);
+            bulk_load(st + kStageData, p.k_cache + static_cast<int64_t>(ti.p0) * kPageBytes + kPageDataBytes,
                       kScaleBytes, &full[s]);
-            if (npg == 2) {
-              tma_load_2d_hint(st + kPageDataBytes, &kmap, &full[s], 0, p1 * kPageRows, policy);
+            if (ti.npg == 2)
               bulk_load(st + kStageData + kScaleBytes,
-                        p.k_cache + static_cast<int64_t>(p1) * kPageBytes + kPageDataBytes,
+                        p.k_cache + static_cast<int64_t>(ti.p1) * kPageBytes + kPageDataBytes,
                         kScaleBytes, &full[s]);
-            }
           }
         }
-        cur_b = b;
-        if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      __syncwarp();
     }
     if (lane == 0) {  // let every copy this thread issued land before the CTA can exit
       for (int64_t k = (n > kStages ? n - kStages : 0); k < n; ++k)
@@ -321,7 +329,7 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
       umma_commit(drain);
       mbar_drain(drain, 0);
     }
-  } else {
+  } else if (warp >= 2 && warp < 2 + kEpiWarps) {
     // ------------------------------------------------------ epilogue warps
     const int sp = warp & 3;          // TMEM sub-partition this warp may access
     const int row = sp * 32 + lane;   // token row of the 128-token tile
@@ -563,14 +571,24 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     int need = K - res[1];
     int count = res[2];
     // One pass: higher bins are winners; the boundary bin becomes candidates.
+    // Eight independent loads per thread are in flight at a time.
     const int Lr = (L + 31) & ~31;
-    for (int i = tid; i < Lr; i += kSelThreads) {
-      const bool in = i < L;
-      const float s = in ? row[i] : 0.f;
-      const uint32_t d = score_key(s) >> 21;
-      const uint64_t c = composite(s, i);
-      warp_append(in && d > bin1, c, sel, &counters[0], kTopK);
-      warp_append(in && d == bin1, c, cand, &counters[1], kCandCap);
+    for (int i0 = 0; i0 < Lr; i0 += 8 * kSelThreads) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kSelThreads + tid;
+        v[u] = i < L ? row[i] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kSelThreads + tid;
+        const bool in = i < L;
+        const uint32_t d = score_key(v[u]) >> 21;
+        const uint64_t c = composite(v[u], i);
+        warp_append(in && d > bin1, c, sel, &counters[0], kTopK);
+        warp_append(in && d == bin1, c, cand, &counters[1], kCandCap);
+      }
     }
     __syncthreads();
     const int ncand = counters[1];
