@@ -33,8 +33,8 @@
 //   A token fully covered by one CTA is normalised and written directly;
 //   otherwise each covering CTA writes an (O, m, l) partial and bumps a
 //   per-token counter; the last one to arrive merges them:
-//   lse = log2 sum_i l_i 2^(m_i - M) + M, out = sum_i O_i 2^(m_i - M) / l,
-//   and resets the counter (so the workspace stays ready for the next call).
+//   lse = log2 sum_i l_i 2^(m_i - M) + M, out = sum_i O_i 2^(m_i - M) / l.
+//   The counters are cleared by an async memset at the start of every call.
 #include <cuda_bf16.h>
 
 #include <cmath>
@@ -88,7 +88,7 @@ struct Params {
   float* lse;
   float* part_o;   // [records][16][512]
   float* part_ml;  // [records][16][2]
-  int* tok_count;  // [num_tokens] partials written so far, zero between calls
+  int* tok_count;  // [num_tokens] partials written so far (cleared at every call)
   unsigned int* status;
   int64_t num_slots;
   int num_tokens;
@@ -575,7 +575,6 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
           if (e == 0) {
             const int prev = atomicAdd(p.tok_count + t, 1);
             const int last = prev == parts_of(t, total, gridDim.x) - 1;
-            if (last) p.tok_count[t] = 0;
             *rescale_flag = last ? 2 : 0;  // reuse the flag word as a broadcast
           }
           named_barrier_sync(1, 128);
@@ -699,6 +698,9 @@ extern "C" int dsa_attention_run(const void* q_nope, const void* q_pe, const voi
   prm.scale_log2 = sm_scale * 1.4426950408889634f;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(prm.tok_count, 0, sizeof(int) * static_cast<size_t>(num_tokens), s) !=
+      cudaSuccess)
+    return DSA_ERR_CUDA;
   attn::attention_kernel<<<grid, attn::kThreads, attn::kSmemBytes, s>>>(ckv_map, kpe_map, qn_map,
                                                                        qp_map, prm);
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;

@@ -15,9 +15,11 @@
 //                  resolved 32 tiles at a time, one group ahead, so no load
 //                  latency sits between two copy issues.  Nothing is dequantised in HBM
 //                  (the reference writes an fp32 copy of K, kernel.py:108-135).
-//      warp 1      MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 tokens,
-//                  N = 64 heads, K = 128 (4 x K32), fp32 accumulator in TMEM,
-//                  4 accumulator stages.
+//      warps 1,7   MMA issuers (even / odd tiles): tcgen05.mma kind::f8f6f4,
+//                  M = 128 tokens, N = 64 heads, K = 128 (4 x K32), fp32
+//                  accumulator in TMEM, 4 accumulator stages.  The issuing
+//                  warp moves the tile's scales into a 4-slot ring so the K
+//                  stage is freed as soon as the MMAs complete.
 //      warps 2-5   epilogue: each thread owns one token row of the TMEM
 //                  accumulator (64 head columns) and computes
 //                  sum_h w_h * relu(scale_tok * acc_h) in registers -- no
@@ -31,7 +33,7 @@
 //    encodes "score descending, then lower token index first" as one total
 //    order.  The score kernel's epilogue already histograms the top 11 key
 //    bits per request (per-warp shared-memory histograms flushed into a
-//    global [batch, 2048] table, which the select kernel zeroes after use);
+//    global [batch, 2048] table, cleared by an async memset at each call);
 //    one pass over the L scores then moves the winners of higher bins to the
 //    output and the boundary bin to a shared-memory candidate list, which
 //    later passes refine.  The 2048
@@ -58,8 +60,9 @@ constexpr int kStageStride = kStageData + 1024;           // + the two pages' sc
 constexpr int kStages = 8;
 constexpr int kAccStages = 4;
 constexpr int kTmemCols = kAccStages * kHeads;            // 256
-constexpr int kThreads = 224;                            // 7 warps
+constexpr int kThreads = 256;                            // 8 warps
 constexpr int kScaleWarp = 6;                           // second producer: scale copies
+constexpr int kMmaWarp2 = 7;                            // second MMA issuer (odd tiles)
 constexpr int kEpiWarps = 4;
 constexpr int kBins = 2048;                               // radix bins: top 11 key bits
 constexpr int kMaxBatch = 4096;
@@ -72,8 +75,9 @@ constexpr uint32_t kIdesc = idesc_make(0, 0, false, false, 128, 64);
 constexpr int kOffStage = 0;
 constexpr int kOffQ = kOffStage + kStages * kStageStride;         // 139264
 constexpr int kOffHist = kOffQ + 2 * kPageDataBytes;              // 155648
-constexpr int kOffBar = kOffHist + kEpiWarps * kBins * 4;         // 188416
-constexpr int kNumBars = 2 * kStages + 4 + 2 * kAccStages + 1;
+constexpr int kOffScale = kOffHist + kEpiWarps * kBins * 4;       // 188416: scale ring
+constexpr int kOffBar = kOffScale + kAccStages * 2 * kScaleBytes; // 190464
+constexpr int kNumBars = 2 * kStages + 4 + 2 * kAccStages + 2;
 constexpr int kOffMisc = kOffBar + 256;
 constexpr int kOffInfo = kOffMisc + 64;                           // 2 producer warps x 32 tiles
 constexpr int kOffTiles = kOffInfo + 2 * 32 * 5 * 4;
@@ -89,7 +93,7 @@ struct ScoreParams {
   const int32_t* seq_lens;
   const int32_t* block_table;
   float* scores;          // [batch][score_stride]
-  unsigned int* hist;     // [batch][kBins], zero on entry, cleared by the select kernel
+  unsigned int* hist;     // [batch][kBins], cleared by an async memset at every call
   unsigned int* status;
   int64_t num_pages;
   int batch;
@@ -184,10 +188,15 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
     // A stage is free again once its MMAs completed (1 commit) and every
     // epilogue warp has read the stage's token scales (4 arrivals).
     // full: one arrive.expect_tx from each producer warp (data, scales).
-    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 2); mbar_init(&empty[s], 1 + kEpiWarps); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&qfull[s], 1); mbar_init(&qempty[s], 1); }
-    for (int s = 0; s < kAccStages; ++s) { mbar_init(&accfull[s], 1); mbar_init(&accempty[s], kEpiWarps); }
-    mbar_init(drain, 1);
+    // empty: the MMA commit (the issuing warp has already copied the
+    // stage's scales into the scale ring).  qempty: one commit from each MMA
+    // issuer.  accfull: the MMA commit plus the issuer's arrive publishing
+    // the scale ring entry.
+    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 2); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&qfull[s], 1); mbar_init(&qempty[s], 2); }
+    for (int s = 0; s < kAccStages; ++s) { mbar_init(&accfull[s], 2); mbar_init(&accempty[s], kEpiWarps); }
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -293,41 +302,67 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         mbar_drain(&full[k % kStages], static_cast<uint32_t>((k / kStages) & 1));
       for (int k = (nq > 2 ? nq - 2 : 0); k < nq; ++k) mbar_drain(&qfull[k & 1], (k >> 1) & 1);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------ MMA issuer
-    if (lane == 0 && u0 < u1) {
+  } else if (warp == 1 || warp == kMmaWarp2) {
+    // ------------------------------------------------------ MMA issuers
+    // Warp 1 takes the even tiles, warp 7 the odd ones: one thread issues
+    // tcgen05.mma at a fixed rate (about 135 cycles per instruction here),
+    // so two issuing warps halve the issue time per tile.  Before the MMAs,
+    // the warp copies the tile's 512 bytes of token scales into the
+    // scale-ring slot of its accumulator stage, so the K stage is released as
+    // soon as the MMAs have read it.
+    const int parity = warp == 1 ? 0 : 1;
+    uint8_t* scale_ring = smem + kOffScale;
+    if (u0 < u1) {
       int cur_b = -1, nq = 0, slot = 0, b = 0, j = 0;
       locate(tile_off, p.batch, u0, b, j);
       int64_t n = 0;
-      for (int64_t u = u0; u < u1; ++u, ++n) {
+      bool ok = true;
+      for (int64_t u = u0; u < u1 && ok; ++u, ++n) {
         if (b != cur_b) {
           cur_b = b;
-          if (nq > 0) umma_commit(&qempty[(nq - 1) & 1]);
+          if (lane == 0) {
+            if (nq > 0) umma_commit(&qempty[(nq - 1) & 1]);
+            ok = mbar_wait(&qfull[nq & 1], (nq >> 1) & 1, wctx);
+          }
           slot = nq & 1;
-          if (!mbar_wait(&qfull[slot], (nq >> 1) & 1, wctx)) break;
           ++nq;
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
         }
-        const int s = static_cast<int>(n % kStages);
-        const uint32_t ph = static_cast<uint32_t>((n / kStages) & 1);
-        const int a = static_cast<int>(n % kAccStages);
-        const uint32_t aph = static_cast<uint32_t>((n / kAccStages) & 1);
-        if (!mbar_wait(&full[s], ph, wctx)) break;
-        if (!mbar_wait(&accempty[a], aph ^ 1, wctx)) break;
-        tc_fence_after();
-        const uint64_t ad = sdesc_sw128(smem_u32(stage_mem + s * kStageStride), 16, 1024);
-        const uint64_t bd = sdesc_sw128(smem_u32(q_mem + slot * kPageDataBytes), 16, 1024);
+        if ((n & 1) == parity) {
+          const int s = static_cast<int>(n % kStages);
+          const uint32_t ph = static_cast<uint32_t>((n / kStages) & 1);
+          const int a = static_cast<int>(n % kAccStages);
+          const uint32_t aph = static_cast<uint32_t>((n / kAccStages) & 1);
+          // Every lane acquires the stage (it reads the bulk-copied scales).
+          ok = mbar_wait(&full[s], ph, wctx) && mbar_wait(&accempty[a], aph ^ 1, wctx);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          // 512 bytes of scales: 16 bytes per lane.
+          const uint4 v = *reinterpret_cast<const uint4*>(stage_mem + s * kStageStride + kStageData + 16 * lane);
+          *reinterpret_cast<uint4*>(scale_ring + a * 2 * kScaleBytes + 16 * lane) = v;
+          __syncwarp();
+          if (lane == 0) {
+            tc_fence_after();
+            const uint64_t ad = sdesc_sw128(smem_u32(stage_mem + s * kStageStride), 16, 1024);
+            const uint64_t bd = sdesc_sw128(smem_u32(q_mem + slot * kPageDataBytes), 16, 1024);
 #pragma unroll
-        for (int k = 0; k < kDim / 32; ++k)  // +32 bytes along K per step (start address >> 4)
-          umma_f8(tmem_base + a * kHeads, ad + 2 * k, bd + 2 * k, kIdesc, k > 0 ? 1u : 0u);
-        umma_commit(&empty[s]);
-        umma_commit(&accfull[a]);
+            for (int k = 0; k < kDim / 32; ++k)  // +32 bytes along K per step (start address >> 4)
+              umma_f8(tmem_base + a * kHeads, ad + 2 * k, bd + 2 * k, kIdesc, k > 0 ? 1u : 0u);
+            umma_commit(&empty[s]);
+            umma_commit(&accfull[a]);
+            mbar_arrive(&accfull[a]);  // publishes this warp's scale-ring stores
+          }
+        }
         if (++j == tile_off[b + 1] - tile_off[b]) {
           j = 0;
           do { ++b; } while (b < p.batch && tile_off[b + 1] == tile_off[b]);
         }
       }
-      umma_commit(drain);
-      mbar_drain(drain, 0);
+      if (lane == 0) {
+        umma_commit(&drain[parity]);
+        mbar_drain(&drain[parity], 0);
+      }
     }
   } else if (warp >= 2 && warp < 2 + kEpiWarps) {
     // ------------------------------------------------------ epilogue warps
@@ -359,18 +394,12 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         }
         const int tok = j * kTileTok + row;
         const bool valid = tok < L;
-        const int s = static_cast<int>(n % kStages);
         const int a = static_cast<int>(n % kAccStages);
         const uint32_t aph = static_cast<uint32_t>((n / kAccStages) & 1);
-        // accfull implies the stage's data landed; waiting on the stage's own
-        // barrier too makes the bulk-copied scales visible to this thread.
-        // (The stage cannot be refilled before this warp arrives on empty[s].)
-        bool good = mbar_wait(&accfull[a], aph, wctx);
-        good = good && mbar_wait(&full[s], static_cast<uint32_t>((n / kStages) & 1), wctx);
-        if (!__all_sync(0xffffffffu, good)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(&accfull[a], aph, wctx))) break;
         tc_fence_after();
         const float scale = *reinterpret_cast<const float*>(
-            stage_mem + s * kStageStride + kStageData + (row >> 6) * kScaleBytes + (row & 63) * 4);
+            smem + kOffScale + a * 2 * kScaleBytes + (row >> 6) * kScaleBytes + (row & 63) * 4);
         float acc[kHeads];
         {
           float lo[32], hi[32];
@@ -383,7 +412,7 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) { mbar_arrive(&accempty[a]); mbar_arrive(&empty[s]); }
+        if (lane == 0) mbar_arrive(&accempty[a]);
         if (valid) {
           // relu(v) written as the reference does: v <= 0 ? 0 : v (NaN passes).
           float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
@@ -557,8 +586,8 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
   unsigned int* ghist = p.hist + static_cast<int64_t>(b) * kBins;
   const int K = L < kTopK ? L : kTopK;
 
-  // Take the histogram the score kernel accumulated, and leave zeros behind.
-  for (int i = tid; i < kBins; i += kSelThreads) { hist[i] = ghist[i]; ghist[i] = 0; }
+  // The histogram the score kernel accumulated for this request.
+  for (int i = tid; i < kBins; i += kSelThreads) hist[i] = ghist[i];
   if (tid == 0) { counters[0] = 0; counters[1] = 0; }
   __syncthreads();
 
@@ -713,6 +742,9 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
   if (st != DSA_OK) return st;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(static_cast<uint8_t*>(workspace) + kWorkspaceHeader, 0,
+                      sizeof(uint32_t) * static_cast<size_t>(batch) * ix::kBins, s) != cudaSuccess)
+    return DSA_ERR_CUDA;
   ix::ScoreParams sp;
   sp.k_cache = static_cast<const uint8_t*>(k_index_cache_fp8);
   sp.weights = weights;

@@ -81,11 +81,10 @@ DSA_API int dsa_b200_abi_version(void);
 DSA_API const char* dsa_b200_status_string(int status);
 
 /* Bytes of device workspace dsa_indexer_run needs for this batch and block
- * table width: a 256-byte header, a [batch, 2048] uint32 radix histogram and
- * [batch, max_pages*64] fp32 score rows.  The workspace must be zero-filled
- * before its first use; every completed call leaves the histogram region
- * zero again, so it can be reused without clearing (re-zero it after a call
- * that raised DSA_DEV_WAIT_TIMEOUT). */
+ * table width: a 256-byte header, a [batch, 2048] uint32 radix histogram
+ * (cleared by the call itself with an async memset) and [batch,
+ * max_pages*64] fp32 score rows.  Zero-fill a workspace once before its first
+ * use so the status word in its header starts clear. */
 DSA_API size_t dsa_indexer_workspace_bytes(int32_t batch, int32_t max_pages);
 
 /* FP8 lightning indexer, decode (one query token per request).
@@ -111,7 +110,10 @@ DSA_API int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cache_f
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* Bytes of device workspace dsa_attention_run needs for num_tokens queries
- * on this device (256-byte header + split-softmax partial records). */
+ * on this device: a 256-byte header, the split-softmax partial records and
+ * one merge counter per token (cleared by the call with an async memset).
+ * Zero-fill a workspace once before its first use so the status word in its
+ * header starts clear. */
 DSA_API size_t dsa_attention_workspace_bytes(int32_t num_tokens);
 
 /* Sparse MLA attention, one query token per row of sparse_indices.

@@ -141,3 +141,12 @@ def test_graph_capture(cuda_device):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, out2) and torch.equal(lse, lse2)
+
+
+def test_workspace_reuse_across_sizes(cuda_device):
+    # One stream, one workspace, token counts that move the merge counters
+    # onto bytes a previous call used for partial records.
+    for T, seed in ((64, 31), (3, 32), (20, 33), (1, 34), (64, 35)):
+        a = workloads.make_attention_inputs(T, pool_pages=2048, seed=seed, device=cuda_device)
+        out, lse = run_gpu(a)
+        check(a, out, lse, tokens=list(range(0, T, max(1, T // 6))) + [T - 1])

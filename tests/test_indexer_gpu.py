@@ -191,3 +191,13 @@ def test_long_context_config2(cuda_device):
         pages = set(bt[b, : (lens[b] + 63) // 64].tolist())
         assert set((row // 64).tolist()) <= pages, b
     print(f"config2 sample: exact {rep.exact_rows}/3, swaps {rep.swaps}")
+
+
+def test_workspace_reuse_across_sizes(cuda_device):
+    # One stream, one workspace; growing the batch at a fixed workspace size
+    # moves the histogram region onto bytes that held scores before.
+    # Largest first, so later calls reuse (never regrow) the workspace.
+    for lens, mp in (([5000] * 9, 80), ([9000] * 2, 160), ([6000] * 6, 100), ([2100] * 4, 160)):
+        ix = workloads.make_indexer_inputs(lens, pool_pages=512, seed=len(lens), device=cuda_device,
+                                           max_pages=mp)
+        oracle_check(ix, run_gpu(ix))
