@@ -31,6 +31,8 @@ SIGNATURES = {
                                          ctypes.c_float, _P, _P, _P, ctypes.c_size_t, _P]),
     "dsa_read_device_status": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int,
                                               _P]),
+    "dsa_indexer_run_noalloc": (ctypes.c_int, [_P, _P, ctypes.c_int64, _P, _P, _P, ctypes.c_int32,
+                                               ctypes.c_int32, _P, _P]),
 }
 
 _lib = None

@@ -136,6 +136,35 @@ DSA_API int dsa_attention_run(const void* q_nope, const void* q_pe,
                       void* output, float* lse,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the scratch array compiled into the library for
+ * dsa_indexer_run_noalloc: the 256-byte header, 64 radix histograms and
+ * 1,048,576 fp32 score slots (4.5 MiB per GPU that loads the library). */
+#define DSA_NOALLOC_SCRATCH_BYTES (256u + 64u * 2048u * 4u + 1048576u * 4u)
+
+/* dsa_indexer_run without a workspace argument, for callers that cannot
+ * allocate device memory when they call: hosts that reach this library
+ * through C / JNI / FFI while another allocator owns the device memory, and
+ * serving loops that allow no cudaMalloc after warm-up.  Scratch comes from
+ * a fixed array inside the library (DSA_NOALLOC_SCRATCH_BYTES), so the
+ * problem must fit: dsa_indexer_workspace_bytes(batch, max_pages) may not
+ * exceed it (e.g. 64 requests x 256 pages, or 8 requests x 2048 pages);
+ * otherwise the call returns DSA_ERR_WORKSPACE_TOO_SMALL before touching the
+ * device.  Nothing is allocated or freed.
+ *   - The first call on a device looks up the array's device address, so
+ *     make it before capturing any stream.
+ *   - All calls share the one array: calls whose work overlaps on the GPU
+ *     (other streams, other threads) race and corrupt each other's results.
+ *   - Data-dependent device errors are recorded in the array's status word,
+ *     which this entry point gives no way to read; use dsa_indexer_run when
+ *     they must be observed.
+ * Arguments have the meaning of dsa_indexer_run.  No counterpart in the
+ * reference, which always allocates its scratch through PyTorch. */
+DSA_API int dsa_indexer_run_noalloc(const void* q_index_fp8, const void* k_index_cache_fp8,
+                                    int64_t num_pages, const float* weights,
+                                    const int32_t* seq_lens, const int32_t* block_table,
+                                    int32_t batch, int32_t max_pages, int32_t* topk_indices,
+                                    void* stream);
+
 /* Copies the sticky device status word of `workspace` to *status_out
  * (synchronising `stream`), and zeroes it when `clear` is non-zero.
  * No counterpart in the reference, which has no error channel
