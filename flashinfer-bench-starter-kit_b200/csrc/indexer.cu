@@ -448,13 +448,16 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
 
 // ------------------------------------------------------------ top-k select
 constexpr int kSelThreads = 1024;
+constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kTopK = DSA_TOPK;
-constexpr int kCandCap = 16384;
-constexpr size_t kSelSmem = sizeof(uint64_t) * (kTopK + kCandCap) + sizeof(uint32_t) * kBins + 256;
+constexpr int kStageCap = 512;                        // staged keys per warp
+constexpr int kStageTotal = kSelWarps * kStageCap;    // 16384
+constexpr size_t kSelSmem = sizeof(uint64_t) * (kTopK + kStageTotal) + sizeof(uint32_t) * kBins +
+                            sizeof(int) * (32 + 8 + kSelWarps);
 
 struct SelectParams {
   const float* scores;
-  unsigned int* hist;
+  const unsigned int* hist;
   const int32_t* seq_lens;
   const int32_t* block_table;
   int32_t* out;
@@ -504,7 +507,9 @@ __device__ __forceinline__ void find_bin(const uint32_t* hist, int need, int* wa
   __syncthreads();
 }
 
-// Appends v to buf when pred holds; one shared atomic per warp.
+// Appends v to buf when pred holds; one shared atomic per warp.  Used only on
+// the fallback path, where a degenerate score distribution overflows the
+// per-warp staging areas.
 __device__ __forceinline__ void warp_append(bool pred, uint64_t v, uint64_t* buf, int* counter,
                                             int cap) {
   const unsigned m = __ballot_sync(0xffffffffu, pred);
@@ -518,77 +523,93 @@ __device__ __forceinline__ void warp_append(bool pred, uint64_t v, uint64_t* buf
   if (pred && pos < cap) buf[pos] = v;
 }
 
-// 64-bit compare-exchange steps of a descending bitonic sort whose partner
-// lives in another lane of the same warp (distance j in 2..32 elements, two
-// elements per thread at 2t and 2t+1).
 __device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int m) {
   const uint32_t lo = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v), m);
   const uint32_t hi = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), m);
   return (static_cast<uint64_t>(hi) << 32) | lo;
 }
 
-__device__ __forceinline__ void reg_steps(uint64_t& x0, uint64_t& x1, int k, int jmax) {
+// Descending sort of the 2048 unique keys in buf (tmp: 2048 more slots).
+// Each warp sorts 64 keys in registers (bitonic, 2 per lane); then five
+// merge-path levels merge runs of 64, 128, ... 1024 keys, every thread
+// producing 2 outputs per level with one 16-byte store.  Every thread of the
+// block must call it; returns the buffer that holds the result.
+__device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp) {
   const int t = threadIdx.x;
-  for (int j = jmax; j >= 1; j >>= 1) {
-    if (j == 1) {
-      const bool desc = ((2 * t) & k) == 0;
-      if (desc ? (x0 < x1) : (x0 > x1)) { const uint64_t tmp = x0; x0 = x1; x1 = tmp; }
-    } else {
-      const uint64_t y0 = shfl_xor64(x0, j >> 1), y1 = shfl_xor64(x1, j >> 1);
-      const int i0 = 2 * t;
-      const bool lo_side = (i0 & j) == 0;
-      const bool desc = (i0 & k) == 0;
-      const bool keep_max = lo_side == desc;
-      x0 = keep_max ? (x0 > y0 ? x0 : y0) : (x0 < y0 ? x0 : y0);
-      x1 = keep_max ? (x1 > y1 ? x1 : y1) : (x1 < y1 ? x1 : y1);
+  const int lane = t & 31;
+  uint64_t x0 = buf[2 * t], x1 = buf[2 * t + 1];
+#pragma unroll
+  for (int kk = 1; kk <= 6; ++kk) {
+    const int k = 1 << kk;
+#pragma unroll
+    for (int jj = kk - 1; jj >= 0; --jj) {
+      const int j = 1 << jj;
+      const int i0 = 2 * lane;                       // position inside the warp's 64
+      const bool desc = k == 64 || (i0 & k) == 0;    // the last stage sorts all descending
+      if (j == 1) {
+        if (desc ? (x0 < x1) : (x0 > x1)) { const uint64_t tt = x0; x0 = x1; x1 = tt; }
+      } else {
+        const uint64_t y0 = shfl_xor64(x0, j >> 1), y1 = shfl_xor64(x1, j >> 1);
+        const bool keep_max = ((i0 & j) == 0) == desc;
+        x0 = keep_max ? (x0 > y0 ? x0 : y0) : (x0 < y0 ? x0 : y0);
+        x1 = keep_max ? (x1 > y1 ? x1 : y1) : (x1 < y1 ? x1 : y1);
+      }
     }
   }
-}
-
-__device__ void bitonic_sort_desc_2048(uint64_t* sel) {
-  const int t = threadIdx.x;
-  uint64_t x0 = sel[2 * t], x1 = sel[2 * t + 1];
-  for (int k = 2; k <= 64; k <<= 1) reg_steps(x0, x1, k, k >> 1);
-  sel[2 * t] = x0; sel[2 * t + 1] = x1;
+  uint64_t* src = buf;
+  uint64_t* dst = tmp;
+  *reinterpret_cast<ulonglong2*>(src + 2 * t) = make_ulonglong2(x0, x1);
   __syncthreads();
-  for (int k = 128; k <= kTopK; k <<= 1) {
-    for (int j = k >> 1; j >= 64; j >>= 1) {
-      const int lo = 2 * j * (t / j) + (t % j);
-      const int hi = lo + j;
-      const uint64_t a = sel[lo], b = sel[hi];
-      const bool desc = (lo & k) == 0;
-      if (desc ? (a < b) : (a > b)) { sel[lo] = b; sel[hi] = a; }
-      __syncthreads();
+#pragma unroll 1
+  for (int R = 64; R < kTopK; R <<= 1) {
+    const int o = 2 * t;                 // first of this thread's two outputs
+    const int pair = o / (2 * R);
+    const int d = o - pair * 2 * R;      // diagonal inside the pair
+    const uint64_t* A = src + pair * 2 * R;
+    const uint64_t* B = A + R;
+    // number of A keys among the d largest of A u B
+    int lo = d > R ? d - R : 0, hi = d < R ? d : R;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (A[mid] > B[d - 1 - mid]) lo = mid + 1; else hi = mid;
     }
-    x0 = sel[2 * t]; x1 = sel[2 * t + 1];
-    reg_steps(x0, x1, k, 32);
-    sel[2 * t] = x0; sel[2 * t + 1] = x1;
+    int ia = lo, ib = d - lo;
+    const bool take_a = ib >= R || (ia < R && A[ia] > B[ib]);
+    const uint64_t r0 = take_a ? A[ia] : B[ib];
+    ia += take_a ? 1 : 0;
+    ib += take_a ? 0 : 1;
+    const bool take_a2 = ib >= R || (ia < R && A[ia] > B[ib]);
+    const uint64_t r1 = take_a2 ? A[ia] : B[ib];
+    *reinterpret_cast<ulonglong2*>(dst + o) = make_ulonglong2(r0, r1);
     __syncthreads();
+    uint64_t* sw = src; src = dst; dst = sw;
   }
+  return src;
 }
 
 __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const SelectParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint64_t* sel = reinterpret_cast<uint64_t*>(smem_raw);
-  uint64_t* cand = sel + kTopK;
-  uint32_t* hist = reinterpret_cast<uint32_t*>(cand + kCandCap);
+  uint64_t* stage = sel + kTopK;
+  uint32_t* hist = reinterpret_cast<uint32_t*>(stage + kStageTotal);
   int* warp_tot = reinterpret_cast<int*>(hist + kBins);  // 32 ints
-  int* res = warp_tot + 32;                               // bin, above, count
-  int* counters = res + 4;                                // nsel, ncand
+  int* res = warp_tot + 32;                               // bin, above, count, overflow, nsel
+  int* wcnt = res + 8;                                    // staged keys per warp
 
   const int b = blockIdx.x;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
+  const int warp = tid >> 5;
   const int max_len = p.max_pages * kPage;
   int L = __ldg(p.seq_lens + b);
   L = L < 0 ? 0 : (L > max_len ? max_len : L);  // the score kernel flags bad lengths
   const float* row = p.scores + static_cast<int64_t>(b) * p.score_stride;
-  unsigned int* ghist = p.hist + static_cast<int64_t>(b) * kBins;
+  const unsigned int* ghist = p.hist + static_cast<int64_t>(b) * kBins;
   const int K = L < kTopK ? L : kTopK;
 
   // The histogram the score kernel accumulated for this request.
   for (int i = tid; i < kBins; i += kSelThreads) hist[i] = ghist[i];
-  if (tid == 0) { counters[0] = 0; counters[1] = 0; }
+  if (tid == 0) { res[3] = 0; res[4] = 0; }
   __syncthreads();
 
   if (L <= kTopK) {
@@ -599,29 +620,47 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     const uint32_t bin1 = static_cast<uint32_t>(res[0]);
     int need = K - res[1];
     int count = res[2];
-    // One pass: higher bins are winners; the boundary bin becomes candidates.
-    // Eight independent loads per thread are in flight at a time.
-    const int Lr = (L + 31) & ~31;
-    for (int i0 = 0; i0 < Lr; i0 += 8 * kSelThreads) {
-      float v[8];
+    // One pass over the scores: every key whose top 11 bits are >= bin1 goes
+    // to this warp's private staging area (warp-uniform counter in a
+    // register: no shared atomics).  key >= bin1 << 21 is one float compare
+    // against the float with that key (NaN ranks highest).  Each thread
+    // loads 4 float4 (16 scores) per round.
+    const uint32_t tkey = bin1 << 21;
+    const float thr = __uint_as_float((tkey & 0x80000000u) ? (tkey & 0x7FFFFFFFu) : ~tkey);
+    const float4* row4 = reinterpret_cast<const float4*>(row);
+    const int L4 = (L + 3) >> 2;                         // float4s covering [0, L)
+    uint64_t* mine = stage + warp * kStageCap;
+    int wcount = 0;
+    for (int q0 = 0; q0 < L4; q0 += 4 * kSelThreads) {
+      float4 v[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + u * kSelThreads + tid;
-        v[u] = i < L ? row[i] : 0.f;
+      for (int u = 0; u < 4; ++u) {
+        const int q = q0 + u * kSelThreads + tid;
+        v[u] = q < L4 ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + u * kSelThreads + tid;
-        const bool in = i < L;
-        const uint32_t d = score_key(v[u]) >> 21;
-        const uint64_t c = composite(v[u], i);
-        warp_append(in && d > bin1, c, sel, &counters[0], kTopK);
-        warp_append(in && d == bin1, c, cand, &counters[1], kCandCap);
+      for (int u = 0; u < 4; ++u) {
+        const int q = q0 + u * kSelThreads + tid;
+        const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int i = 4 * q + c;
+          const bool pred = i < L && (e[c] >= thr || e[c] != e[c]);
+          const unsigned m = __ballot_sync(0xffffffffu, pred);
+          if (m) {
+            const int pos = wcount + __popc(m & ((1u << lane) - 1u));
+            if (pred && pos < kStageCap) mine[pos] = composite(e[c], i);
+            wcount += __popc(m);
+          }
+        }
       }
     }
+    if (lane == 0) {
+      wcnt[warp] = wcount;
+      if (wcount > kStageCap) atomicOr(&res[3], 1);
+    }
     __syncthreads();
-    const int ncand = counters[1];
-    const bool in_smem = ncand <= kCandCap;
+    const bool staged = res[3] == 0;
     uint64_t prefix = static_cast<uint64_t>(bin1) << 53;
     uint64_t mask = static_cast<uint64_t>(0x7FF) << 53;
     // Refine the boundary: 11-bit digits of the remaining 53 key bits.
@@ -632,10 +671,12 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
       const uint64_t dm = (static_cast<uint64_t>(1) << widths[pass]) - 1;
       for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
       __syncthreads();
-      if (in_smem) {
-        for (int i = tid; i < ncand; i += kSelThreads) {
-          const uint64_t c = cand[i];
-          if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
+      if (staged) {
+        for (int i = tid; i < kStageTotal; i += kSelThreads) {
+          if ((i & (kStageCap - 1)) < wcnt[i / kStageCap]) {
+            const uint64_t c = stage[i];
+            if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
+          }
         }
       } else {
         for (int i = tid; i < L; i += kSelThreads) {
@@ -650,32 +691,45 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
       need -= res[1];
       count = res[2];
     }
-    // Collect the boundary-bin winners: (c & mask) >= prefix.
-    if (in_smem) {
-      const int nr = (ncand + 31) & ~31;
-      for (int i = tid; i < nr; i += kSelThreads) {
-        const uint64_t c = i < ncand ? cand[i] : 0ull;
-        warp_append(i < ncand && (c & mask) >= prefix, c, sel, &counters[0], kTopK);
+    // The K winners are the keys with (c & mask) >= prefix.
+    if (staged) {
+      // Lane l of warp w owns slots l + 32k of the warp's area (no bank
+      // conflicts): count, block scan, write.
+      const uint64_t* area = stage + warp * kStageCap;
+      const int avail = wcnt[warp];
+      int cnt = 0;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int j = lane + 32 * k;
+        cnt += (j < avail && (area[j] & mask) >= prefix) ? 1 : 0;
+      }
+      const int incl = block_scan_incl(cnt, warp_tot);
+      int pos = incl - cnt;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int j = lane + 32 * k;
+        const uint64_t c = area[j];
+        if (j < avail && (c & mask) >= prefix) sel[pos++] = c;
       }
     } else {
+      const int Lr = (L + 31) & ~31;
       for (int i = tid; i < Lr; i += kSelThreads) {
         const bool in = i < L;
         const uint64_t c = in ? composite(row[i], i) : 0ull;
-        warp_append(in && (c >> 53) == bin1 && (c & mask) >= prefix, c, sel, &counters[0], kTopK);
+        warp_append(in && (c & mask) >= prefix, c, sel, &res[4], kTopK);
       }
     }
     __syncthreads();
   }
-  (void)lane;
 
-  bitonic_sort_desc_2048(sel);
+  const uint64_t* sorted = sort_desc_2048(sel, stage);
 
   int32_t* out = p.out + static_cast<int64_t>(b) * kTopK;
   const int32_t* bt = p.block_table + static_cast<int64_t>(b) * p.max_pages;
   for (int i = tid; i < kTopK; i += kSelThreads) {
     int32_t v = -1;
     if (i < K) {
-      const int tok = static_cast<int>(~static_cast<uint32_t>(sel[i]));
+      const int tok = static_cast<int>(~static_cast<uint32_t>(sorted[i]));
       v = __ldg(bt + (tok >> 6)) * kPage + (tok & 63);
     }
     out[i] = v;
