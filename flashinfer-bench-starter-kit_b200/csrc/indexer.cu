@@ -7,23 +7,24 @@
 //    concatenation over requests of 128-token tiles (two 64-token pages);
 //    CTA c takes the contiguous slice [c*U/G, (c+1)*U/G) of the U tiles, so
 //    load balance does not depend on how seq_lens are distributed.  Roles:
-//      warps 0,6   TMA producers: raw FP8 pages (64 rows x 128 B, 128-byte
-//                  swizzle; warp 0) and each page's 64 fp32 scales (bulk
-//                  copy; warp 6) straight from the paged cache into an
-//                  8-deep shared-memory ring, and q[b] (64 heads x 128 B)
-//                  when the request changes.  Block-table entries are
+//      warps 8,9   TMA producers, each owning every 2nd tile: raw FP8 pages
+//                  (64 rows x 128 B, 128-byte swizzle) and each page's 64
+//                  fp32 scales (bulk copy) straight from the paged cache into
+//                  an 8-deep shared-memory ring.  Block-table entries are
 //                  resolved 32 tiles at a time, one group ahead, so no load
 //                  latency sits between two copy issues.  Nothing is dequantised in HBM
 //                  (the reference writes an fp32 copy of K, kernel.py:108-135).
-//      warps 1,7   MMA issuers (even / odd tiles): tcgen05.mma kind::f8f6f4,
+//      warps 10,11 MMA issuers (even / odd tiles; warp 10 also loads q[b],
+//                  64 heads x 128 B, when the request changes): tcgen05.mma kind::f8f6f4,
 //                  M = 128 tokens, N = 64 heads, K = 128 (4 x K32), fp32
 //                  accumulator in TMEM, 4 accumulator stages.  The issuing
 //                  warp moves the tile's scales into a 4-slot ring so the K
 //                  stage is freed as soon as the MMAs complete.
-//      warps 2-5   epilogue: each thread owns one token row of the TMEM
-//                  accumulator (64 head columns) and computes
-//                  sum_h w_h * relu(scale_tok * acc_h) in registers -- no
-//                  cross-thread reduction -- then stores one fp32 score.
+//      warps 0-7   epilogue, two sets of four (even / odd tiles): each
+//                  thread owns one token row of the TMEM accumulator (64
+//                  head columns) and computes sum_h w_h * relu(scale_tok *
+//                  acc_h) in registers -- no cross-thread reduction -- then
+//                  stores one fp32 score.
 //    Scores go to a [batch, max_pages*64] fp32 workspace (L2-resident at
 //    decode sizes); per-head scores never exist in memory (the reference
 //    materialises [64, L] fp32, kernel.py:293-300).
@@ -60,10 +61,12 @@ constexpr int kStageStride = kStageData + 1024;           // + the two pages' sc
 constexpr int kStages = 8;
 constexpr int kAccStages = 4;
 constexpr int kTmemCols = kAccStages * kHeads;            // 256
-constexpr int kThreads = 256;                            // 8 warps
-constexpr int kScaleWarp = 6;                           // second producer: scale copies
-constexpr int kMmaWarp2 = 7;                            // second MMA issuer (odd tiles)
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;                              // warps 0-7: epilogue, two sets of 4
+constexpr int kHists = 4;                                 // one per TMEM sub-partition
+constexpr int kProdWarp0 = kEpiWarps;                     // warps 8-9: producers
+constexpr int kProdWarps = 2;
+constexpr int kMmaWarp0 = kProdWarp0 + kProdWarps;        // warps 10-11: MMA issuers
+constexpr int kThreads = 32 * (kMmaWarp0 + 2);            // 12 warps
 constexpr int kBins = 2048;                               // radix bins: top 11 key bits
 constexpr int kMaxBatch = 4096;
 constexpr int kMaxPagesPerSeq = 1 << 20;
@@ -75,13 +78,15 @@ constexpr uint32_t kIdesc = idesc_make(0, 0, false, false, 128, 64);
 constexpr int kOffStage = 0;
 constexpr int kOffQ = kOffStage + kStages * kStageStride;         // 139264
 constexpr int kOffHist = kOffQ + 2 * kPageDataBytes;              // 155648
-constexpr int kOffScale = kOffHist + kEpiWarps * kBins * 4;       // 188416: scale ring
+constexpr int kOffScale = kOffHist + kHists * kBins * 4;          // 188416: scale ring
 constexpr int kOffBar = kOffScale + kAccStages * 2 * kScaleBytes; // 190464
 constexpr int kNumBars = 2 * kStages + 4 + 2 * kAccStages + 2;
 constexpr int kOffMisc = kOffBar + 256;
-constexpr int kOffInfo = kOffMisc + 64;                           // 2 producer warps x 32 tiles
-constexpr int kOffTiles = kOffInfo + 2 * 32 * 5 * 4;
+constexpr int kOffInfo = kOffMisc + 64;                           // 4 producer warps x 32 tiles
+constexpr int kOffTiles = kOffInfo + kProdWarps * 32 * 5 * 4;
 static_assert(kNumBars * 8 <= 256, "barrier area");
+static_assert(16 + 4 * (kThreads / 32) <= 64, "misc area");
+static_assert(kAccStages % 2 == 0, "epilogue sets take alternate accumulator stages");
 
 inline size_t score_smem_bytes(int batch) {
   return 1024 + kOffTiles + sizeof(int) * static_cast<size_t>(batch + 1);
@@ -176,7 +181,7 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   uint64_t* drain = accempty + kAccStages;
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + kOffMisc + 4);
-  int* warp_sums = reinterpret_cast<int*>(smem + kOffMisc + 16);  // 6 ints
+  int* warp_sums = reinterpret_cast<int*>(smem + kOffMisc + 16);  // one int per warp
   int* tile_off = reinterpret_cast<int*>(smem + kOffTiles);
 
   const int tid = threadIdx.x;
@@ -185,25 +190,23 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   const int max_len = p.max_pages * kPage;
 
   if (tid == 0) {
-    // A stage is free again once its MMAs completed (1 commit) and every
-    // epilogue warp has read the stage's token scales (4 arrivals).
-    // full: one arrive.expect_tx from each producer warp (data, scales).
-    // empty: the MMA commit (the issuing warp has already copied the
-    // stage's scales into the scale ring).  qempty: one commit from each MMA
-    // issuer.  accfull: the MMA commit plus the issuer's arrive publishing
-    // the scale ring entry.
-    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 2); mbar_init(&empty[s], 1); }
+    // full: the owning producer warp's arrive.expect_tx.  accempty: the four
+    // epilogue warps of the set that owns the stage.  empty: the MMA
+    // commit (the issuing warp has already copied the stage's scales into the
+    // scale ring).  qempty: one commit from each MMA issuer.  accfull: the
+    // MMA commit plus the issuer's arrive publishing the scale ring entry.
+    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int s = 0; s < 2; ++s) { mbar_init(&qfull[s], 1); mbar_init(&qempty[s], 2); }
-    for (int s = 0; s < kAccStages; ++s) { mbar_init(&accfull[s], 2); mbar_init(&accempty[s], kEpiWarps); }
+    for (int s = 0; s < kAccStages; ++s) { mbar_init(&accfull[s], 2); mbar_init(&accempty[s], 4); }
     mbar_init(&drain[0], 1);
     mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) { prefetch_tensor_map(&kmap); prefetch_tensor_map(&qmap); }
-  if (warp == 1) tmem_alloc(tmem_base_smem, kTmemCols);
-  if (warp >= 2) {  // zero the per-warp histograms
-    for (int i = tid - 64; i < kEpiWarps * kBins; i += 128) hist_all[i] = 0;
+  if (warp == kProdWarp0 && lane == 0) { prefetch_tensor_map(&kmap); prefetch_tensor_map(&qmap); }
+  if (warp == kMmaWarp0) tmem_alloc(tmem_base_smem, kTmemCols);
+  if (warp < kEpiWarps) {  // zero the shared-memory histograms
+    for (int i = tid; i < kHists * kBins; i += 32 * kEpiWarps) hist_all[i] = 0;
   }
 
   // Tile prefix sums over requests (each CTA recomputes them: seq_lens stay
@@ -244,53 +247,41 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   const int64_t u1 = total * (blockIdx.x + 1) / gridDim.x;
   const WaitCtx wctx{abort_flag, p.status};
 
-  if (warp == 0 || warp == kScaleWarp) {
+  if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
     // ------------------------------------------------------ producer warps
-    // Warp 0 issues the two FP8 page boxes of each tile (and q[b] when the
-    // request changes); warp 6 issues the two 256-byte scale copies.  A
-    // thread issues TMA / bulk copies at a fixed rate, so splitting the four
-    // copies of a tile over two warps halves the issue time per tile.  Each
-    // warp resolves the block-table entries of 32 tiles at once, one group
-    // ahead, and stages them in shared memory for its issuing lane.
-    const bool data_warp = warp == 0;
-    TileInfo* info = reinterpret_cast<TileInfo*>(smem + kOffInfo) + (data_warp ? 0 : 32);
+    // Warp 8+k owns tiles n = k, k+2, k+4, ... of this CTA's slice and issues
+    // both of their FP8 page boxes and both 256-byte scale copies.  One thread
+    // issues copies at a fixed rate, so two producer warps keep the ring
+    // full.  Each warp resolves the block-table entries of its next 32 tiles
+    // at once, one group ahead, and stages them in shared memory.
+    const int k = warp - kProdWarp0;
+    TileInfo* info = reinterpret_cast<TileInfo*>(smem + kOffInfo) + 32 * k;
     const uint64_t policy = make_policy_evict_first();
-    int cur_b = -1, nq = 0;
-    int64_t n = 0;
+    const int64_t mine = (u1 - u0 > k) ? (u1 - u0 - k + kProdWarps - 1) / kProdWarps : 0;
+    int64_t m = 0;  // tiles issued by this warp
     int ok = 1;
-    TileInfo nxt = tile_info(p, tile_off, u0 + lane, u1, max_len);
-    for (int64_t g0 = u0; g0 < u1 && ok; g0 += 32) {
+    TileInfo nxt = tile_info(p, tile_off, u0 + k + kProdWarps * lane, u1, max_len);
+    for (int64_t g0 = 0; g0 < mine && ok; g0 += 32) {
       info[lane] = nxt;
-      nxt = tile_info(p, tile_off, g0 + 32 + lane, u1, max_len);  // one group ahead
+      nxt = tile_info(p, tile_off, u0 + k + kProdWarps * (g0 + 32 + lane), u1, max_len);
       __syncwarp();
-      const int cnt = static_cast<int>(u1 - g0 < 32 ? u1 - g0 : 32);
+      const int cnt = static_cast<int>(mine - g0 < 32 ? mine - g0 : 32);
       if (lane == 0) {
-        for (int t = 0; t < cnt; ++t, ++n) {
+        for (int t = 0; t < cnt; ++t, ++m) {
           const TileInfo ti = info[t];
-          if (data_warp && ti.b != cur_b) {
-            const int slot = nq & 1;
-            if (!mbar_wait(&qempty[slot], ((nq >> 1) & 1) ^ 1, wctx)) { ok = 0; break; }
-            mbar_arrive_expect_tx(&qfull[slot], kPageDataBytes);
-            tma_load_2d(q_mem + slot * kPageDataBytes, &qmap, &qfull[slot], 0, ti.b * kHeads);
-            ++nq;
-          }
-          cur_b = ti.b;
+          const int64_t n = k + kProdWarps * m;  // tile index within the CTA
           const int s = static_cast<int>(n % kStages);
           if (!mbar_wait(&empty[s], static_cast<uint32_t>(((n / kStages) & 1) ^ 1), wctx)) { ok = 0; break; }
           uint8_t* st = stage_mem + s * kStageStride;
-          if (data_warp) {
-            mbar_arrive_expect_tx(&full[s], ti.npg * kPageDataBytes);
-            tma_load_2d_hint(st, &kmap, &full[s], 0, ti.p0 * kPageRows, policy);
-            if (ti.npg == 2)
-              tma_load_2d_hint(st + kPageDataBytes, &kmap, &full[s], 0, ti.p1 * kPageRows, policy);
-          } else {
-            mbar_arrive_expect_tx(&full[s], ti.npg * kScaleBytes);
-            bulk_load(st + kStageData, p.k_cache + static_cast<int64_t>(ti.p0) * kPageBytes + kPageDataBytes,
+          mbar_arrive_expect_tx(&full[s], ti.npg * (kPageDataBytes + kScaleBytes));
+          tma_load_2d_hint(st, &kmap, &full[s], 0, ti.p0 * kPageRows, policy);
+          bulk_load(st + kStageData, p.k_cache + static_cast<int64_t>(ti.p0) * kPageBytes + kPageDataBytes,
+                    kScaleBytes, &full[s]);
+          if (ti.npg == 2) {
+            tma_load_2d_hint(st + kPageDataBytes, &kmap, &full[s], 0, ti.p1 * kPageRows, policy);
+            bulk_load(st + kStageData + kScaleBytes,
+                      p.k_cache + static_cast<int64_t>(ti.p1) * kPageBytes + kPageDataBytes,
                       kScaleBytes, &full[s]);
-            if (ti.npg == 2)
-              bulk_load(st + kStageData + kScaleBytes,
-                        p.k_cache + static_cast<int64_t>(ti.p1) * kPageBytes + kPageDataBytes,
-                        kScaleBytes, &full[s]);
           }
         }
       }
@@ -298,19 +289,20 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
       __syncwarp();
     }
     if (lane == 0) {  // let every copy this thread issued land before the CTA can exit
-      for (int64_t k = (n > kStages ? n - kStages : 0); k < n; ++k)
-        mbar_drain(&full[k % kStages], static_cast<uint32_t>((k / kStages) & 1));
-      for (int k = (nq > 2 ? nq - 2 : 0); k < nq; ++k) mbar_drain(&qfull[k & 1], (k >> 1) & 1);
+      for (int64_t j = (m > 2 ? m - 2 : 0); j < m; ++j) {
+        const int64_t n = k + kProdWarps * j;
+        mbar_drain(&full[n % kStages], static_cast<uint32_t>((n / kStages) & 1));
+      }
     }
-  } else if (warp == 1 || warp == kMmaWarp2) {
+  } else if (warp >= kMmaWarp0) {
     // ------------------------------------------------------ MMA issuers
-    // Warp 1 takes the even tiles, warp 7 the odd ones: one thread issues
+    // Warp 10 takes the even tiles, warp 11 the odd ones: one thread issues
     // tcgen05.mma at a fixed rate (about 135 cycles per instruction here),
     // so two issuing warps halve the issue time per tile.  Before the MMAs,
     // the warp copies the tile's 512 bytes of token scales into the
     // scale-ring slot of its accumulator stage, so the K stage is released as
     // soon as the MMAs have read it.
-    const int parity = warp == 1 ? 0 : 1;
+    const int parity = warp - kMmaWarp0;
     uint8_t* scale_ring = smem + kOffScale;
     if (u0 < u1) {
       int cur_b = -1, nq = 0, slot = 0, b = 0, j = 0;
@@ -322,7 +314,14 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
           cur_b = b;
           if (lane == 0) {
             if (nq > 0) umma_commit(&qempty[(nq - 1) & 1]);
-            ok = mbar_wait(&qfull[nq & 1], (nq >> 1) & 1, wctx);
+            if (parity == 0) {  // warp 10 loads q[b] once both issuers released the slot
+              ok = mbar_wait(&qempty[nq & 1], ((nq >> 1) & 1) ^ 1, wctx);
+              if (ok) {
+                mbar_arrive_expect_tx(&qfull[nq & 1], kPageDataBytes);
+                tma_load_2d(q_mem + (nq & 1) * kPageDataBytes, &qmap, &qfull[nq & 1], 0, b * kHeads);
+              }
+            }
+            ok = ok && mbar_wait(&qfull[nq & 1], (nq >> 1) & 1, wctx);
           }
           slot = nq & 1;
           ++nq;
@@ -362,27 +361,40 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
       if (lane == 0) {
         umma_commit(&drain[parity]);
         mbar_drain(&drain[parity], 0);
+        if (parity == 0)  // a q load still in flight must land before exit
+          for (int j = (nq > 2 ? nq - 2 : 0); j < nq; ++j) mbar_drain(&qfull[j & 1], (j >> 1) & 1);
       }
     }
-  } else if (warp >= 2 && warp < 2 + kEpiWarps) {
+  } else {
     // ------------------------------------------------------ epilogue warps
+    // Two sets of four warps take the even and the odd tiles (so the even and
+    // odd accumulator stages), which gives every scheduler two epilogue warps
+    // to interleave.  Warp w reads TMEM sub-partition w & 3, token rows
+    // 32*(w&3) .. +31.  The two warps of a sub-partition share a histogram and
+    // flush it together when the request changes; both step through every
+    // tile of the slice so they meet at the same flushes, and a warp whose
+    // wait gave up keeps stepping (without work) so its partner is not left
+    // at a barrier.
+    const int set = warp >> 2;
     const int sp = warp & 3;          // TMEM sub-partition this warp may access
     const int row = sp * 32 + lane;   // token row of the 128-token tile
-    uint32_t* hist = hist_all + (warp - 2) * kBins;
+    uint32_t* hist = hist_all + sp * kBins;
     if (u0 < u1) {
       int b = 0, j = 0;
       locate(tile_off, p.batch, u0, b, j);
       int cur_b = -1, L = 0;
       float wt[kHeads];
       int64_t n = 0;
-      // Adds this warp's histogram of request `fb` into the global one.
+      bool live = true;
+      // Adds request `fb`'s counts into the global histogram; each warp of
+      // the pair moves half of the bins.
       auto flush = [&](int fb) {
-        __syncwarp();
-        for (int i = lane; i < kBins; i += 32) {
+        named_barrier_sync(1 + sp, 64);
+        for (int i = set * (kBins / 2) + lane; i < (set + 1) * (kBins / 2); i += 32) {
           const uint32_t v = hist[i];
           if (v) { atomicAdd(p.hist + static_cast<int64_t>(fb) * kBins + i, v); hist[i] = 0; }
         }
-        __syncwarp();
+        named_barrier_sync(1 + sp, 64);
       };
       for (int64_t u = u0; u < u1; ++u, ++n) {
         if (b != cur_b) {
@@ -392,42 +404,54 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
 #pragma unroll
           for (int h = 0; h < kHeads; ++h) wt[h] = __ldg(p.weights + cur_b * kHeads + h);
         }
-        const int tok = j * kTileTok + row;
-        const bool valid = tok < L;
-        const int a = static_cast<int>(n % kAccStages);
-        const uint32_t aph = static_cast<uint32_t>((n / kAccStages) & 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(&accfull[a], aph, wctx))) break;
-        tc_fence_after();
-        const float scale = *reinterpret_cast<const float*>(
-            smem + kOffScale + a * 2 * kScaleBytes + (row >> 6) * kScaleBytes + (row & 63) * 4);
-        float acc[kHeads];
-        {
-          float lo[32], hi[32];
-          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + a * kHeads;
-          tmem_ld32(taddr, lo);
-          tmem_ld32(taddr + 32, hi);
-          tmem_wait_ld();
+        if ((n & 1) == set && live) {
+          const int tok = j * kTileTok + row;
+          const int a = static_cast<int>(n % kAccStages);
+          const uint32_t aph = static_cast<uint32_t>((n / kAccStages) & 1);
+          live = __all_sync(0xffffffffu, mbar_wait(&accfull[a], aph, wctx));
+          if (live) {
+            tc_fence_after();
+            const float scale = *reinterpret_cast<const float*>(
+                smem + kOffScale + a * 2 * kScaleBytes + (row >> 6) * kScaleBytes + (row & 63) * 4);
+            float lo[32], hi[32];
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + a * kHeads;
+            tmem_ld32(taddr, lo);
+            tmem_ld32(taddr + 32, hi);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&accempty[a]);
+            if (tok < L) {
+              float sc;
+              if (scale > 0.f) {
+                // relu(scale * v) = scale * relu(v) for scale > 0: one max
+                // (NaN-propagating, as the reference's v <= 0 ? 0 : v) and
+                // one fma per head.
+                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-          for (int h = 0; h < 32; ++h) { acc[h] = lo[h]; acc[h + 32] = hi[h]; }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&accempty[a]);
-        if (valid) {
-          // relu(v) written as the reference does: v <= 0 ? 0 : v (NaN passes).
-          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                for (int h = 0; h < 32; h += 2) {
+                  s0 = fmaf(relu_nan(lo[h]), wt[h], s0);
+                  s1 = fmaf(relu_nan(lo[h + 1]), wt[h + 1], s1);
+                  s2 = fmaf(relu_nan(hi[h]), wt[h + 32], s2);
+                  s3 = fmaf(relu_nan(hi[h + 1]), wt[h + 33], s3);
+                }
+                sc = scale * ((s0 + s1) + (s2 + s3));
+              } else {
+                // Zero, negative or NaN scale: relu(scale * v) term by term,
+                // written as the reference does (v <= 0 ? 0 : v).
+                float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-          for (int h = 0; h < kHeads; h += 4) {
-            float x0 = acc[h] * scale, x1 = acc[h + 1] * scale;
-            float x2 = acc[h + 2] * scale, x3 = acc[h + 3] * scale;
-            s0 += (x0 <= 0.f ? 0.f : x0) * wt[h];
-            s1 += (x1 <= 0.f ? 0.f : x1) * wt[h + 1];
-            s2 += (x2 <= 0.f ? 0.f : x2) * wt[h + 2];
-            s3 += (x3 <= 0.f ? 0.f : x3) * wt[h + 3];
+                for (int h = 0; h < 32; ++h) {
+                  const float x0 = lo[h] * scale, x1 = hi[h] * scale;
+                  s0 += (x0 <= 0.f ? 0.f : x0) * wt[h];
+                  s1 += (x1 <= 0.f ? 0.f : x1) * wt[h + 32];
+                }
+                sc = s0 + s1;
+              }
+              p.scores[static_cast<int64_t>(cur_b) * p.score_stride + tok] = sc;
+              atomicAdd(&hist[score_key(sc) >> 21], 1u);
+            }
           }
-          const float sc = (s0 + s1) + (s2 + s3);
-          p.scores[static_cast<int64_t>(cur_b) * p.score_stride + tok] = sc;
-          atomicAdd(&hist[score_key(sc) >> 21], 1u);
         }
         if (++j == tile_off[b + 1] - tile_off[b]) {
           j = 0;
@@ -440,7 +464,7 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }

@@ -312,6 +312,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 }
 
 // ---------------------------------------------------------------- misc
+// max(x, 0) that returns NaN for a NaN input (max.NaN), i.e. the value of
+// x <= 0 ? 0 : x up to the sign of a zero result.
+__device__ __forceinline__ float relu_nan(float x) {
+  float y;
+  asm("max.NaN.f32 %0, %1, 0f00000000;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Order-preserving map of an fp32 score to uint32: larger key == larger
 // score; every NaN maps to the largest key (torch.topk ranks NaN first) and
 // -0.0 to the key of +0.0.
