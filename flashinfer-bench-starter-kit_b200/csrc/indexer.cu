@@ -8,18 +8,18 @@
 //    CTA c takes the contiguous slice [c*U/G, (c+1)*U/G) of the U tiles, so
 //    load balance does not depend on how seq_lens are distributed.  Roles:
 //      warps 8,9   TMA producers, each owning every 2nd tile: raw FP8 pages
-//                  (64 rows x 128 B, 128-byte swizzle) and each page's 64
-//                  fp32 scales (bulk copy) straight from the paged cache into
-//                  an 8-deep shared-memory ring.  Block-table entries are
+//                  (64 rows x 128 B, 128-byte swizzle) into an 8-deep
+//                  shared-memory ring and each page's 64 fp32 scales (bulk
+//                  copy) into a 12-slot scale ring that outlives the K stage
+//                  until the epilogue has used it.  Block-table entries are
 //                  resolved 32 tiles at a time, one group ahead, so no load
 //                  latency sits between two copy issues.  Nothing is dequantised in HBM
 //                  (the reference writes an fp32 copy of K, kernel.py:108-135).
 //      warps 10,11 MMA issuers (even / odd tiles; warp 10 also loads q[b],
 //                  64 heads x 128 B, when the request changes): tcgen05.mma kind::f8f6f4,
 //                  M = 128 tokens, N = 64 heads, K = 128 (4 x K32), fp32
-//                  accumulator in TMEM, 4 accumulator stages.  The issuing
-//                  warp moves the tile's scales into a 4-slot ring so the K
-//                  stage is freed as soon as the MMAs complete.
+//                  accumulator in TMEM, 4 accumulator stages; the K stage is
+//                  freed as soon as the MMAs complete.
 //      warps 0-7   epilogue, two sets of four (even / odd tiles): each
 //                  thread owns one token row of the TMEM accumulator (64
 //                  head columns) and computes sum_h w_h * relu(scale_tok *
@@ -57,17 +57,26 @@ constexpr int kPageDataBytes = kPage * kDim;              // 8192
 constexpr int kScaleBytes = kPage * 4;                    // 256
 constexpr int kTileTok = 2 * kPage;                       // 128 tokens per tile
 constexpr int kStageData = 2 * kPageDataBytes;            // 16384: two pages of FP8 rows
-constexpr int kStageStride = kStageData + 1024;           // + the two pages' scales, 1 KiB aligned
+constexpr int kStageStride = kStageData;                  // 1 KiB aligned (128-byte swizzle atoms)
 constexpr int kStages = 8;
 constexpr int kAccStages = 4;
 constexpr int kTmemCols = kAccStages * kHeads;            // 256
+// Token-scale ring: tile n's 2 x 64 fp32 scales go to slot n % kScaleSlots.
+// The producer of tile n waited for the MMAs of tile n - kStages, which
+// waited for the epilogue of tile n - kStages - kAccStages to release its
+// accumulator (after reading its scales), so that slot is free again.
+constexpr int kScaleSlots = kStages + kAccStages;
 constexpr int kEpiWarps = 8;                              // warps 0-7: epilogue, two sets of 4
-constexpr int kHists = 4;                                 // one per TMEM sub-partition
 constexpr int kProdWarp0 = kEpiWarps;                     // warps 8-9: producers
 constexpr int kProdWarps = 2;
-constexpr int kMmaWarp0 = kProdWarp0 + kProdWarps;        // warps 10-11: MMA issuers
-constexpr int kThreads = 32 * (kMmaWarp0 + 2);            // 12 warps
+constexpr int kMmaWarp0 = kProdWarp0 + kProdWarps;        // warps 10-13: MMA issuers
+constexpr int kMmaWarps = 4;
+constexpr int kThreads = 32 * (kMmaWarp0 + kMmaWarps);    // 14 warps
 constexpr int kBins = 2048;                               // radix bins: top 11 key bits
+// Each epilogue warp keeps its own histogram of 16-bit counters, two per
+// word, and flushes it at least every kFlushEvery of its tiles: 32 lanes x
+// 2047 tiles < 65536, so a counter never carries into its neighbour.
+constexpr int kFlushEvery = 2047;
 constexpr int kMaxBatch = 4096;
 constexpr int kMaxPagesPerSeq = 1 << 20;
 constexpr int64_t kMaxPool = (int64_t(1) << 31) / kPageRows - 1;
@@ -76,17 +85,19 @@ constexpr int64_t kMaxPool = (int64_t(1) << 31) / kPageRows - 1;
 constexpr uint32_t kIdesc = idesc_make(0, 0, false, false, 128, 64);
 
 constexpr int kOffStage = 0;
-constexpr int kOffQ = kOffStage + kStages * kStageStride;         // 139264
-constexpr int kOffHist = kOffQ + 2 * kPageDataBytes;              // 155648
-constexpr int kOffScale = kOffHist + kHists * kBins * 4;          // 188416: scale ring
-constexpr int kOffBar = kOffScale + kAccStages * 2 * kScaleBytes; // 190464
-constexpr int kNumBars = 2 * kStages + 4 + 2 * kAccStages + 2;
+constexpr int kOffQ = kOffStage + kStages * kStageStride;         // 131072
+constexpr int kOffHist = kOffQ + 2 * kPageDataBytes;              // 147456
+constexpr int kOffScale = kOffHist + kEpiWarps * kBins * 2;       // 180224: scale ring
+constexpr int kOffBar = kOffScale + kScaleSlots * 2 * kScaleBytes; // 186368
+constexpr int kNumBars = 2 * kStages + 4 + 2 * kAccStages + kMmaWarps;
 constexpr int kOffMisc = kOffBar + 256;
-constexpr int kOffInfo = kOffMisc + 64;                           // 4 producer warps x 32 tiles
+constexpr int kOffInfo = kOffMisc + 128;                          // producer warps x 32 tiles
 constexpr int kOffTiles = kOffInfo + kProdWarps * 32 * 5 * 4;
 static_assert(kNumBars * 8 <= 256, "barrier area");
-static_assert(16 + 4 * (kThreads / 32) <= 64, "misc area");
+static_assert(kStages % kProdWarps == 0 && kScaleSlots % kProdWarps == 0, "producer stride");
+static_assert(16 + 4 * (kThreads / 32) <= 128, "misc area");
 static_assert(kAccStages % 2 == 0, "epilogue sets take alternate accumulator stages");
+static_assert((kMmaWarps & (kMmaWarps - 1)) == 0, "MMA issuers split tiles by n % kMmaWarps");
 
 inline size_t score_smem_bytes(int batch) {
   return 1024 + kOffTiles + sizeof(int) * static_cast<size_t>(batch + 1);
@@ -166,8 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap qmap, const ScoreParams p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  // Pointer arithmetic on the shared array (not an integer round trip) keeps
+  // the shared address space visible to the compiler: plain LDS/STS/ATOMS.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* stage_mem = smem + kOffStage;
   uint8_t* q_mem = smem + kOffQ;
   uint32_t* hist_all = reinterpret_cast<uint32_t*>(smem + kOffHist);
@@ -192,21 +204,19 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   if (tid == 0) {
     // full: the owning producer warp's arrive.expect_tx.  accempty: the four
     // epilogue warps of the set that owns the stage.  empty: the MMA
-    // commit (the issuing warp has already copied the stage's scales into the
-    // scale ring).  qempty: one commit from each MMA issuer.  accfull: the
-    // MMA commit plus the issuer's arrive publishing the scale ring entry.
+    // commit.  qempty: one commit from each MMA issuer.  accfull: the MMA
+    // commit plus the issuer's arrive, which publishes the scale-ring entry.
     for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&qfull[s], 1); mbar_init(&qempty[s], 2); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&qfull[s], 1); mbar_init(&qempty[s], kMmaWarps); }
     for (int s = 0; s < kAccStages; ++s) { mbar_init(&accfull[s], 2); mbar_init(&accempty[s], 4); }
-    mbar_init(&drain[0], 1);
-    mbar_init(&drain[1], 1);
+    for (int w = 0; w < kMmaWarps; ++w) mbar_init(&drain[w], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == kProdWarp0 && lane == 0) { prefetch_tensor_map(&kmap); prefetch_tensor_map(&qmap); }
   if (warp == kMmaWarp0) tmem_alloc(tmem_base_smem, kTmemCols);
   if (warp < kEpiWarps) {  // zero the shared-memory histograms
-    for (int i = tid; i < kHists * kBins; i += 32 * kEpiWarps) hist_all[i] = 0;
+    for (int i = tid; i < kEpiWarps * kBins / 2; i += 32 * kEpiWarps) hist_all[i] = 0;
   }
 
   // Tile prefix sums over requests (each CTA recomputes them: seq_lens stay
@@ -243,8 +253,9 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
 
   const uint32_t tmem_base = *tmem_base_smem;
   const int64_t total = tile_off[p.batch];
-  const int64_t u0 = total * blockIdx.x / gridDim.x;
-  const int64_t u1 = total * (blockIdx.x + 1) / gridDim.x;
+  const int u0 = static_cast<int>(total * blockIdx.x / gridDim.x);
+  const int u1 = static_cast<int>(total * (blockIdx.x + 1) / gridDim.x);
+  const int nt = u1 - u0;  // tiles of this CTA
   const WaitCtx wctx{abort_flag, p.status};
 
   if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
@@ -257,208 +268,210 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
     const int k = warp - kProdWarp0;
     TileInfo* info = reinterpret_cast<TileInfo*>(smem + kOffInfo) + 32 * k;
     const uint64_t policy = make_policy_evict_first();
-    const int64_t mine = (u1 - u0 > k) ? (u1 - u0 - k + kProdWarps - 1) / kProdWarps : 0;
-    int64_t m = 0;  // tiles issued by this warp
+    const int mine = nt > k ? (nt - k + kProdWarps - 1) / kProdWarps : 0;
+    int m = 0;  // tiles issued by this warp
     int ok = 1;
+    // Stage, its phase and the scale slot of this warp's next tile
+    // n = k + kProdWarps * m, advanced incrementally.
+    int s = k, sslot = k;
+    uint32_t ph = 0;
     TileInfo nxt = tile_info(p, tile_off, u0 + k + kProdWarps * lane, u1, max_len);
-    for (int64_t g0 = 0; g0 < mine && ok; g0 += 32) {
+    for (int g0 = 0; g0 < mine && ok; g0 += 32) {
       info[lane] = nxt;
       nxt = tile_info(p, tile_off, u0 + k + kProdWarps * (g0 + 32 + lane), u1, max_len);
       __syncwarp();
-      const int cnt = static_cast<int>(mine - g0 < 32 ? mine - g0 : 32);
+      const int cnt = mine - g0 < 32 ? mine - g0 : 32;
       if (lane == 0) {
         for (int t = 0; t < cnt; ++t, ++m) {
           const TileInfo ti = info[t];
-          const int64_t n = k + kProdWarps * m;  // tile index within the CTA
-          const int s = static_cast<int>(n % kStages);
-          if (!mbar_wait(&empty[s], static_cast<uint32_t>(((n / kStages) & 1) ^ 1), wctx)) { ok = 0; break; }
+          if (!mbar_wait(&empty[s], ph ^ 1, wctx)) { ok = 0; break; }
           uint8_t* st = stage_mem + s * kStageStride;
+          uint8_t* sc = smem + kOffScale + sslot * 2 * kScaleBytes;
           mbar_arrive_expect_tx(&full[s], ti.npg * (kPageDataBytes + kScaleBytes));
           tma_load_2d_hint(st, &kmap, &full[s], 0, ti.p0 * kPageRows, policy);
-          bulk_load(st + kStageData, p.k_cache + static_cast<int64_t>(ti.p0) * kPageBytes + kPageDataBytes,
+          bulk_load(sc, p.k_cache + static_cast<int64_t>(ti.p0) * kPageBytes + kPageDataBytes,
                     kScaleBytes, &full[s]);
           if (ti.npg == 2) {
             tma_load_2d_hint(st + kPageDataBytes, &kmap, &full[s], 0, ti.p1 * kPageRows, policy);
-            bulk_load(st + kStageData + kScaleBytes,
-                      p.k_cache + static_cast<int64_t>(ti.p1) * kPageBytes + kPageDataBytes,
+            bulk_load(sc + kScaleBytes, p.k_cache + static_cast<int64_t>(ti.p1) * kPageBytes + kPageDataBytes,
                       kScaleBytes, &full[s]);
           }
+          if ((s += kProdWarps) >= kStages) { s -= kStages; ph ^= 1; }
+          if ((sslot += kProdWarps) >= kScaleSlots) sslot -= kScaleSlots;
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       __syncwarp();
     }
     if (lane == 0) {  // let every copy this thread issued land before the CTA can exit
-      for (int64_t j = (m > 2 ? m - 2 : 0); j < m; ++j) {
-        const int64_t n = k + kProdWarps * j;
+      for (int j = (m > 2 ? m - 2 : 0); j < m; ++j) {
+        const int n = k + kProdWarps * j;
         mbar_drain(&full[n % kStages], static_cast<uint32_t>((n / kStages) & 1));
       }
     }
   } else if (warp >= kMmaWarp0) {
     // ------------------------------------------------------ MMA issuers
-    // Warp 10 takes the even tiles, warp 11 the odd ones: one thread issues
-    // tcgen05.mma at a fixed rate (about 135 cycles per instruction here),
-    // so two issuing warps halve the issue time per tile.  Before the MMAs,
-    // the warp copies the tile's 512 bytes of token scales into the
-    // scale-ring slot of its accumulator stage, so the K stage is released as
-    // soon as the MMAs have read it.
+    // Warp 10+r takes the tiles n with n % 4 == r.  A thread can hand
+    // tcgen05 and bulk-copy instructions to the asynchronous units only at a
+    // fixed rate (about 135-180 cycles per instruction, paid by its next
+    // shared-memory access), so a tile's 4 MMAs + 2 commits from one thread
+    // take longer than the tile's HBM time; four issuing warps share the
+    // load.  The whole loop runs in lane 0; the other lanes wait at the final
+    // __syncwarp.
     const int parity = warp - kMmaWarp0;
-    uint8_t* scale_ring = smem + kOffScale;
-    if (u0 < u1) {
-      int cur_b = -1, nq = 0, slot = 0, b = 0, j = 0;
+    if (lane == 0 && nt > 0) {
+      int b = 0, j = 0;
       locate(tile_off, p.batch, u0, b, j);
-      int64_t n = 0;
-      bool ok = true;
-      for (int64_t u = u0; u < u1 && ok; ++u, ++n) {
-        if (b != cur_b) {
-          cur_b = b;
-          if (lane == 0) {
-            if (nq > 0) umma_commit(&qempty[(nq - 1) & 1]);
-            if (parity == 0) {  // warp 10 loads q[b] once both issuers released the slot
-              ok = mbar_wait(&qempty[nq & 1], ((nq >> 1) & 1) ^ 1, wctx);
-              if (ok) {
-                mbar_arrive_expect_tx(&qfull[nq & 1], kPageDataBytes);
-                tma_load_2d(q_mem + (nq & 1) * kPageDataBytes, &qmap, &qfull[nq & 1], 0, b * kHeads);
-              }
+      int ntb = tile_off[b + 1] - tile_off[b];  // tiles of request b
+      int nq = 0, slot = 0;
+      int s = 0, a = 0;          // stage and accumulator of tile n
+      uint32_t ph = 0, aph = 0;  // and their phase parities
+      bool ok = true, new_req = true;
+      for (int n = 0; n < nt && ok; ++n) {
+        if (new_req) {
+          new_req = false;
+          if (nq > 0) umma_commit(&qempty[(nq - 1) & 1]);
+          if (parity == 0) {  // warp 10 loads q[b] once all issuers released the slot
+            ok = mbar_wait(&qempty[nq & 1], ((nq >> 1) & 1) ^ 1, wctx);
+            if (ok) {
+              mbar_arrive_expect_tx(&qfull[nq & 1], kPageDataBytes);
+              tma_load_2d(q_mem + (nq & 1) * kPageDataBytes, &qmap, &qfull[nq & 1], 0, b * kHeads);
             }
-            ok = ok && mbar_wait(&qfull[nq & 1], (nq >> 1) & 1, wctx);
           }
+          ok = ok && mbar_wait(&qfull[nq & 1], (nq >> 1) & 1, wctx);
           slot = nq & 1;
           ++nq;
-          ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) break;
         }
-        if ((n & 1) == parity) {
-          const int s = static_cast<int>(n % kStages);
-          const uint32_t ph = static_cast<uint32_t>((n / kStages) & 1);
-          const int a = static_cast<int>(n % kAccStages);
-          const uint32_t aph = static_cast<uint32_t>((n / kAccStages) & 1);
-          // Every lane acquires the stage (it reads the bulk-copied scales).
+        if ((n & (kMmaWarps - 1)) == parity) {
           ok = mbar_wait(&full[s], ph, wctx) && mbar_wait(&accempty[a], aph ^ 1, wctx);
-          ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
-          // 512 bytes of scales: 16 bytes per lane.
-          const uint4 v = *reinterpret_cast<const uint4*>(stage_mem + s * kStageStride + kStageData + 16 * lane);
-          *reinterpret_cast<uint4*>(scale_ring + a * 2 * kScaleBytes + 16 * lane) = v;
-          __syncwarp();
-          if (lane == 0) {
-            tc_fence_after();
-            const uint64_t ad = sdesc_sw128(smem_u32(stage_mem + s * kStageStride), 16, 1024);
-            const uint64_t bd = sdesc_sw128(smem_u32(q_mem + slot * kPageDataBytes), 16, 1024);
+          tc_fence_after();
+          const uint64_t ad = sdesc_sw128(smem_u32(stage_mem + s * kStageStride), 16, 1024);
+          const uint64_t bd = sdesc_sw128(smem_u32(q_mem + slot * kPageDataBytes), 16, 1024);
 #pragma unroll
-            for (int k = 0; k < kDim / 32; ++k)  // +32 bytes along K per step (start address >> 4)
-              umma_f8(tmem_base + a * kHeads, ad + 2 * k, bd + 2 * k, kIdesc, k > 0 ? 1u : 0u);
-            umma_commit(&empty[s]);
-            umma_commit(&accfull[a]);
-            mbar_arrive(&accfull[a]);  // publishes this warp's scale-ring stores
-          }
+          for (int k = 0; k < kDim / 32; ++k)  // +32 bytes along K per step (start address >> 4)
+            umma_f8(tmem_base + a * kHeads, ad + 2 * k, bd + 2 * k, kIdesc, k > 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+          umma_commit(&accfull[a]);
+          // Release after this thread's acquire of full[s]: makes the
+          // tile's bulk-copied token scales visible to the epilogue.
+          mbar_arrive(&accfull[a]);
         }
-        if (++j == tile_off[b + 1] - tile_off[b]) {
+        if (++s == kStages) { s = 0; ph ^= 1; }
+        if (++a == kAccStages) { a = 0; aph ^= 1; }
+        if (++j == ntb) {
           j = 0;
           do { ++b; } while (b < p.batch && tile_off[b + 1] == tile_off[b]);
+          if (b < p.batch) ntb = tile_off[b + 1] - tile_off[b];
+          new_req = true;
         }
       }
-      if (lane == 0) {
-        umma_commit(&drain[parity]);
-        mbar_drain(&drain[parity], 0);
-        if (parity == 0)  // a q load still in flight must land before exit
-          for (int j = (nq > 2 ? nq - 2 : 0); j < nq; ++j) mbar_drain(&qfull[j & 1], (j >> 1) & 1);
-      }
+      umma_commit(&drain[parity]);
+      mbar_drain(&drain[parity], 0);
+      if (parity == 0)  // a q load still in flight must land before exit
+        for (int j = (nq > 2 ? nq - 2 : 0); j < nq; ++j) mbar_drain(&qfull[j & 1], (j >> 1) & 1);
     }
+    __syncwarp();
   } else {
     // ------------------------------------------------------ epilogue warps
     // Two sets of four warps take the even and the odd tiles (so the even and
     // odd accumulator stages), which gives every scheduler two epilogue warps
     // to interleave.  Warp w reads TMEM sub-partition w & 3, token rows
-    // 32*(w&3) .. +31.  The two warps of a sub-partition share a histogram and
-    // flush it together when the request changes; both step through every
-    // tile of the slice so they meet at the same flushes, and a warp whose
-    // wait gave up keeps stepping (without work) so its partner is not left
-    // at a barrier.
+    // 32*(w&3) .. +31, and steps straight from one of its tiles to the next.
     const int set = warp >> 2;
     const int sp = warp & 3;          // TMEM sub-partition this warp may access
     const int row = sp * 32 + lane;   // token row of the 128-token tile
-    uint32_t* hist = hist_all + sp * kBins;
-    if (u0 < u1) {
+    uint32_t* hist = hist_all + warp * (kBins / 2);
+    if (set < nt) {
       int b = 0, j = 0;
-      locate(tile_off, p.batch, u0, b, j);
-      int cur_b = -1, L = 0;
+      locate(tile_off, p.batch, u0 + set, b, j);
+      int ntb = tile_off[b + 1] - tile_off[b];
+      int L = 0;
+      float* srow = nullptr;
       float wt[kHeads];
-      int64_t n = 0;
-      bool live = true;
-      // Adds request `fb`'s counts into the global histogram; each warp of
-      // the pair moves half of the bins.
-      auto flush = [&](int fb) {
-        named_barrier_sync(1 + sp, 64);
-        for (int i = set * (kBins / 2) + lane; i < (set + 1) * (kBins / 2); i += 32) {
-          const uint32_t v = hist[i];
-          if (v) { atomicAdd(p.hist + static_cast<int64_t>(fb) * kBins + i, v); hist[i] = 0; }
-        }
-        named_barrier_sync(1 + sp, 64);
-      };
-      for (int64_t u = u0; u < u1; ++u, ++n) {
-        if (b != cur_b) {
-          if (cur_b >= 0) flush(cur_b);
-          cur_b = b;
-          L = clamp_len(__ldg(p.seq_lens + cur_b), max_len, p.status);
+      auto enter = [&]() {  // request b becomes current
+        L = clamp_len(__ldg(p.seq_lens + b), max_len, p.status);
+        srow = p.scores + static_cast<int64_t>(b) * p.score_stride;
 #pragma unroll
-          for (int h = 0; h < kHeads; ++h) wt[h] = __ldg(p.weights + cur_b * kHeads + h);
+        for (int h = 0; h < kHeads; ++h) wt[h] = __ldg(p.weights + b * kHeads + h);
+      };
+      // Adds the warp's counts (request fb) into the global histogram.
+      auto flush = [&](int fb) {
+        __syncwarp();
+        unsigned int* g = p.hist + static_cast<int64_t>(fb) * kBins;
+        for (int i = lane; i < kBins / 2; i += 32) {
+          const uint32_t w = hist[i];
+          if (w) {
+            if (w & 0xFFFFu) atomicAdd(g + 2 * i, w & 0xFFFFu);
+            if (w >> 16) atomicAdd(g + 2 * i + 1, w >> 16);
+            hist[i] = 0;
+          }
         }
-        if ((n & 1) == set && live) {
-          const int tok = j * kTileTok + row;
-          const int a = static_cast<int>(n % kAccStages);
-          const uint32_t aph = static_cast<uint32_t>((n / kAccStages) & 1);
-          live = __all_sync(0xffffffffu, mbar_wait(&accfull[a], aph, wctx));
-          if (live) {
-            tc_fence_after();
-            const float scale = *reinterpret_cast<const float*>(
-                smem + kOffScale + a * 2 * kScaleBytes + (row >> 6) * kScaleBytes + (row & 63) * 4);
-            float lo[32], hi[32];
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + a * kHeads;
-            tmem_ld32(taddr, lo);
-            tmem_ld32(taddr + 32, hi);
-            tmem_wait_ld();
+        __syncwarp();
+      };
+      enter();
+      int a = set, slot = set, since = 0;  // accumulator, scale slot of tile n
+      uint32_t aph = 0;
+      for (int n = set; n < nt; n += 2) {
+        const int tok = j * kTileTok + row;
+        if (!__all_sync(0xffffffffu, mbar_wait(&accfull[a], aph, wctx))) break;
+        tc_fence_after();
+        const float scale = *reinterpret_cast<const float*>(smem + kOffScale + slot * 2 * kScaleBytes + row * 4);
+        // relu(scale * v) = scale * relu(v) for scale > 0: one max
+        // (NaN-propagating, like the reference's v <= 0 ? 0 : v) and one fma
+        // per head; other scales (zero, negative, NaN) take relu(scale * v)
+        // term by term as the reference writes it.  Two 32-column halves keep
+        // the register footprint small enough for 14 warps.
+        const bool pos = scale > 0.f;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + a * kHeads;
+        float f0 = 0.f, f1 = 0.f, g0 = 0.f;
+        float v[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld32_wait(taddr + 32 * half, v);
+          if (half == 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&accempty[a]);
-            if (tok < L) {
-              float sc;
-              if (scale > 0.f) {
-                // relu(scale * v) = scale * relu(v) for scale > 0: one max
-                // (NaN-propagating, as the reference's v <= 0 ? 0 : v) and
-                // one fma per head.
-                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+          }
+          if (pos) {
 #pragma unroll
-                for (int h = 0; h < 32; h += 2) {
-                  s0 = fmaf(relu_nan(lo[h]), wt[h], s0);
-                  s1 = fmaf(relu_nan(lo[h + 1]), wt[h + 1], s1);
-                  s2 = fmaf(relu_nan(hi[h]), wt[h + 32], s2);
-                  s3 = fmaf(relu_nan(hi[h + 1]), wt[h + 33], s3);
-                }
-                sc = scale * ((s0 + s1) + (s2 + s3));
-              } else {
-                // Zero, negative or NaN scale: relu(scale * v) term by term,
-                // written as the reference does (v <= 0 ? 0 : v).
-                float s0 = 0.f, s1 = 0.f;
+            for (int h = 0; h < 32; h += 2) {
+              f0 = fmaf(relu_nan(v[h]), wt[32 * half + h], f0);
+              f1 = fmaf(relu_nan(v[h + 1]), wt[32 * half + h + 1], f1);
+            }
+          } else {
 #pragma unroll
-                for (int h = 0; h < 32; ++h) {
-                  const float x0 = lo[h] * scale, x1 = hi[h] * scale;
-                  s0 += (x0 <= 0.f ? 0.f : x0) * wt[h];
-                  s1 += (x1 <= 0.f ? 0.f : x1) * wt[h + 32];
-                }
-                sc = s0 + s1;
-              }
-              p.scores[static_cast<int64_t>(cur_b) * p.score_stride + tok] = sc;
-              atomicAdd(&hist[score_key(sc) >> 21], 1u);
+            for (int h = 0; h < 32; ++h) {
+              const float x = v[h] * scale;
+              g0 += (x <= 0.f ? 0.f : x) * wt[32 * half + h];
             }
           }
         }
-        if (++j == tile_off[b + 1] - tile_off[b]) {
-          j = 0;
-          do { ++b; } while (b < p.batch && tile_off[b + 1] == tile_off[b]);
+        if (tok < L) {
+          const float sc = pos ? scale * (f0 + f1) : g0;
+          srow[tok] = sc;
+          const uint32_t bin = score_key(sc) >> 21;
+          atomicAdd(&hist[bin >> 1], 1u << ((bin & 1u) << 4));
+        }
+        // Step to tile n + 2.
+        if ((a += 2) >= kAccStages) { a -= kAccStages; aph ^= 1; }
+        if ((slot += 2) >= kScaleSlots) slot -= kScaleSlots;
+        ++since;
+        if (n + 2 < nt) {
+          if ((j += 2) >= ntb) {
+            flush(b);
+            since = 0;
+            do { j -= ntb; ++b; ntb = tile_off[b + 1] - tile_off[b]; } while (j >= ntb);
+            enter();
+          } else if (since == kFlushEvery) {
+            flush(b);
+            since = 0;
+          }
         }
       }
-      if (cur_b >= 0) flush(cur_b);
+      flush(b);
     }
   }
 

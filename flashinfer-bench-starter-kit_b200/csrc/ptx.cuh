@@ -17,6 +17,7 @@ namespace dsa {
 
 // A pipeline wait gives up after this long and raises DSA_DEV_WAIT_TIMEOUT.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr unsigned int kSuspendHintNs = 20000;               // per try_wait sleep
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -58,6 +59,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with an explicit suspend-time hint: the thread sleeps until the
+// phase completes or about `ns` nanoseconds have passed, instead of spinning
+// and taking issue slots from the warps that do the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return done != 0;
+}
+
 // Non-blocking check that the phase with the given parity has completed.
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   uint32_t done;
@@ -85,15 +101,13 @@ struct WaitCtx {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& ctx) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u) {
-      if (*ctx.abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        *ctx.abort_flag = 1;
-        atomicOr(ctx.status, DSA_DEV_WAIT_TIMEOUT);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
+    if (*ctx.abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *ctx.abort_flag = 1;
+      atomicOr(ctx.status, DSA_DEV_WAIT_TIMEOUT);
+      return false;
     }
   }
 }
@@ -307,6 +321,27 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
         "=r"(r[31])
       : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// tmem_ld32 followed by tcgen05.wait::ld in the same asm statement, so no use
+// of the destination registers can be scheduled before the wait.
+__device__ __forceinline__ void tmem_ld32_wait(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
