@@ -10,24 +10,27 @@
 //   T x 32 tiles of 64 selected rows; CTA c takes the contiguous slice
 //   [c*U/G, (c+1)*U/G) ("stream-K"), so every SM streams the same number of
 //   rows whatever T is.  Roles:
-//     warps 0-3  producers: read the tile's 64 slot ids (one tile ahead) and
+//     warps 4-11 producers: read the tile's 64 slot ids (one tile ahead) and
 //                TMA tile::gather4 the rows' ckv (8 x 128-byte chunks) and
 //                kpe (1 chunk) into a 2-deep ring with 128-byte swizzle.  A
-//                warp issues gather4 ops at a fixed rate, so the 9 chunks are
-//                split over 4 warps (measured: 1 issuing warp caps random-row
-//                gathers near 2 TB/s, 8 warps reach the HBM roofline).
-//                Warp 0 also loads q_nope / q_pe by 2-D TMA per token.
-//     warp 4     MMA issuer (tcgen05, bf16, fp32 accumulators in TMEM),
-//                issuing logits and PV in whatever order their inputs
+//                thread issues gather4 ops at a fixed rate (about 70 cycles
+//                each), so the 144 ops of a tile are split over 8 warps:
+//                warp 4+w takes row half w >> 2 and chunks w&3, (w&3)+4 and,
+//                for w&3 == 0, the kpe chunk.  Warp 4 also loads q_nope / q_pe
+//                by 2-D TMA per token.
+//     warps 12-15 MMA issuers (tcgen05, bf16, fp32 accumulators in TMEM),
+//                each issuing logits and PV in whatever order their inputs
 //                become ready:
 //                  S^T[64 rows, 16 heads]  = K[64, 576] . Q[16, 576]^T
-//                  (M = 64, N = 16, 36 x K16 spread over 4 independent
-//                  partial accumulators, so consecutive MMAs never wait on
-//                  each other's result), then after the softmax
+//                  (M = 64, N = 16, 36 x K16; warp 12+r issues the K16 steps
+//                  k = r (mod 4) into partial accumulator r), then after the
+//                  softmax
 //                  O^T[512, 16] += V^T[512, 64] . P^T[64, 16]
-//                  (4 x M = 128, N = 16, 4 x K16); V^T is the same shared
-//                  memory as the ckv chunks, read MN-major.
-//     warps 5-8  online softmax in base 2 with lazy rescaling (the running
+//                  (M = 128, N = 16, 4 x K16 for V^T block r); V^T is the
+//                  same shared memory as the ckv chunks, read MN-major.  One
+//                  thread hands tcgen05.mma to the tensor core only every
+//                  ~135 cycles, so a tile's 52 MMAs are split four ways.
+//     warps 0-3  online softmax in base 2 with lazy rescaling (the running
 //                max is only moved when a tile exceeds it by more than 8,
 //                so O in TMEM is rarely touched), P^T written as bf16.
 //   A token fully covered by one CTA is normalised and written directly;
@@ -58,10 +61,12 @@ constexpr int kStageBytes = kChunks * kChunkBytes;  // 73728
 constexpr int kQChunkBytes = kHeads * 128;       // 2048
 constexpr int kQBytes = kChunks * kQChunkBytes;  // 18432
 constexpr int kPBytes = kHeads * kRows * 2;      // 2048
-constexpr int kProdWarps = 4;                    // warps 0-3: gather producers
-constexpr int kMmaWarp = 4;                      // warp 4: TMEM owner + MMA issuer
-constexpr int kSoftWarp0 = 5;                    // warps 5-8: online softmax
-constexpr int kThreads = 288;
+constexpr int kSoftWarp0 = 0;                    // warps 0-3: online softmax
+constexpr int kProdWarp0 = 4;                    // warps 4-11: gather producers
+constexpr int kProdWarps = 8;
+constexpr int kMmaWarp0 = 12;                    // warps 12-15: MMA issuers (12 owns TMEM)
+constexpr int kMmaWarps = 4;
+constexpr int kThreads = 512;
 constexpr int kTmemCols = 256;
 constexpr uint32_t kColO = 0;    // O^T buffers at [0,64) and [64,128): 4 blocks x 16 heads
 constexpr uint32_t kColS = 128;  // S^T buffers at [128,192) and [192,256): 4 partial sums x 16 heads
@@ -80,7 +85,7 @@ constexpr int kOffSx = kOffP + 2 * kPBytes;          // 188416
 constexpr int kOffBar = kOffSx + kHeads * kRows * 4; // 192512
 constexpr int kOffMisc = kOffBar + 256;
 constexpr int kSmemBytes = 1024 + kOffMisc + 256;
-static_assert(19 * 8 <= 256, "barrier area");
+static_assert((18 + kMmaWarps) * 8 <= 256, "barrier area");
 
 struct Params {
   const int32_t* indices;
@@ -209,7 +214,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   uint64_t* p_full = bars + 12;
   uint64_t* p_empty = bars + 14;
   uint64_t* o_empty = bars + 16;
-  uint64_t* drain = bars + 18;
+  uint64_t* drain = bars + 18;  // one per MMA warp
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + kOffMisc + 4);
   int* rescale_flag = reinterpret_cast<int*>(smem + kOffMisc + 8);
@@ -222,22 +227,22 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
 
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], kProdWarps); mbar_init(&kv_empty[s], 1);
-      mbar_init(&q_full[s], 1);  mbar_init(&q_empty[s], 1);
-      mbar_init(&s_full[s], 1);  mbar_init(&s_empty[s], 128);
-      mbar_init(&p_full[s], 1);  mbar_init(&p_empty[s], 1);
+      mbar_init(&kv_full[s], kProdWarps); mbar_init(&kv_empty[s], kMmaWarps);
+      mbar_init(&q_full[s], 1);  mbar_init(&q_empty[s], kMmaWarps);
+      mbar_init(&s_full[s], kMmaWarps);  mbar_init(&s_empty[s], 128);
+      mbar_init(&p_full[s], 1);  mbar_init(&p_empty[s], kMmaWarps);
       mbar_init(&o_empty[s], 1);
     }
-    mbar_init(drain, 1);
+    for (int w = 0; w < kMmaWarps; ++w) mbar_init(&drain[w], 1);
     *abort_flag = 0;
     *rescale_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
+  if (warp == kProdWarp0 && lane == 0) {
     prefetch_tensor_map(&ckv_map); prefetch_tensor_map(&kpe_map);
     prefetch_tensor_map(&qn_map);  prefetch_tensor_map(&qp_map);
   }
-  if (warp == kMmaWarp) tmem_alloc(tmem_base_smem, kTmemCols);
+  if (warp == kMmaWarp0) tmem_alloc(tmem_base_smem, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -250,30 +255,31 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   const int t_first = static_cast<int>(u0 / kTilesPerTok);
   const WaitCtx wctx{abort_flag, p.status};
 
-  if (warp < kProdWarps) {
+  if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
     // ------------------------------------------------------ producer warps
-    // Warp w gathers chunks w, w+4, w+8 (ckv 0-7, kpe 8) of every tile.
-    const int nchunks = (kChunks - warp + kProdWarps - 1) / kProdWarps;
+    // Warp 4+w gathers rows 32*(w>>2) .. +31 (lanes 0-7: 4 rows each) of
+    // chunks w&3, (w&3)+4 and, for w&3 == 0, 8 (the kpe chunk).
+    const int w = warp - kProdWarp0;
+    const int half = w >> 2;
+    const int c0 = w & 3;
+    const int nchunks = c0 == 0 ? 3 : 2;
     const uint64_t policy = make_policy_evict_first();
     int nq = 0, i = 0;
-    auto load_idx = [&](int j, int& a, int& b) {
-      a = b = 0;
+    auto load_idx = [&](int j) {
+      int v = 0;
       if (j < n) {
         const int64_t u = u0 + j;
-        const int32_t* r = p.indices + (u / kTilesPerTok) * kTopK + (u % kTilesPerTok) * kRows;
-        a = __ldg(r + 2 * lane);
-        b = __ldg(r + 2 * lane + 1);
+        v = __ldg(p.indices + (u / kTilesPerTok) * kTopK + (u % kTilesPerTok) * kRows + 32 * half + lane);
       }
+      return v;
     };
-    int v0, v1;
-    load_idx(0, v0, v1);
+    int v = load_idx(0);
     for (; i < n; ++i) {
       const int64_t u = u0 + i;
       const int t = static_cast<int>(u / kTilesPerTok);
       const int tile = static_cast<int>(u % kTilesPerTok);
-      int nv0, nv1;
-      load_idx(i + 1, nv0, nv1);  // next tile's slot ids, in flight meanwhile
-      if (warp == 0 && (i == 0 || tile == 0)) {
+      const int nv = load_idx(i + 1);  // next tile's slot ids, in flight meanwhile
+      if (w == 0 && (i == 0 || tile == 0)) {
         const int slot = nq & 1;
         int ok = 1;
         if (lane == 0) {
@@ -290,43 +296,42 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
         ++nq;
       }
       const int s = i & 1;
-      const int r0v = sanitize_slot(v0, p.num_slots, p.status);
-      const int r1v = sanitize_slot(v1, p.num_slots, p.status);
+      const int rv = sanitize_slot(v, p.num_slots, p.status);
       int ok = 1;
       if (lane == 0) {
         ok = mbar_wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, wctx);
-        if (ok) mbar_arrive_expect_tx(&kv_full[s], nchunks * 16 * 512);
+        if (ok) mbar_arrive_expect_tx(&kv_full[s], nchunks * 8 * 512);
       }
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-      const int src = 2 * (lane & 15);
-      const int r0 = __shfl_sync(0xffffffffu, r0v, src);
-      const int r1 = __shfl_sync(0xffffffffu, r1v, src);
-      const int r2 = __shfl_sync(0xffffffffu, r0v, src + 1);
-      const int r3 = __shfl_sync(0xffffffffu, r1v, src + 1);
-      if (lane < 16) {
-        uint8_t* dst = stage_mem + s * kStageBytes + lane * 512;
-        for (int c = warp; c < kChunks; c += kProdWarps) {
-          if (c < 8)
-            tma_gather4(dst + c * kChunkBytes, &ckv_map, &kv_full[s], c * 64, r0, r1, r2, r3, policy);
-          else
-            tma_gather4(dst + c * kChunkBytes, &kpe_map, &kv_full[s], 0, r0, r1, r2, r3, policy);
-        }
+      const int src = 4 * (lane & 7);
+      const int r0 = __shfl_sync(0xffffffffu, rv, src);
+      const int r1 = __shfl_sync(0xffffffffu, rv, src + 1);
+      const int r2 = __shfl_sync(0xffffffffu, rv, src + 2);
+      const int r3 = __shfl_sync(0xffffffffu, rv, src + 3);
+      if (lane < 8) {
+        uint8_t* dst = stage_mem + s * kStageBytes + (8 * half + lane) * 512;
+        tma_gather4(dst + c0 * kChunkBytes, &ckv_map, &kv_full[s], c0 * 64, r0, r1, r2, r3, policy);
+        tma_gather4(dst + (c0 + 4) * kChunkBytes, &ckv_map, &kv_full[s], (c0 + 4) * 64, r0, r1, r2, r3,
+                    policy);
+        if (c0 == 0)
+          tma_gather4(dst + 8 * kChunkBytes, &kpe_map, &kv_full[s], 0, r0, r1, r2, r3, policy);
       }
       __syncwarp();
-      v0 = nv0;
-      v1 = nv1;
+      v = nv;
     }
     if (lane == 0) {  // let in-flight copies land before the CTA can exit
       for (int k = (i > 2 ? i - 2 : 0); k < i; ++k) mbar_drain(&kv_full[k & 1], (k >> 1) & 1);
-      if (warp == 0)
+      if (w == 0)
         for (int k = (nq > 2 ? nq - 2 : 0); k < nq; ++k) mbar_drain(&q_full[k & 1], (k >> 1) & 1);
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------ MMA issuer
+  } else if (warp >= kMmaWarp0) {
+    // ------------------------------------------------------ MMA issuers
     // Logits of tile i need its gathered rows, its token's Q and a free S
     // buffer; PV of tile i needs P(i) (and, at a segment start, a drained O
     // buffer).  Both are polled and issued as soon as ready, so PV(i) never
-    // waits behind the next tile's gather.
+    // waits behind the next tile's gather.  Warp 12+r issues the logits K16
+    // steps k = r (mod 4) (partial accumulator r) and the PV of V^T block r.
+    const int r = warp - kMmaWarp0;
     if (lane == 0 && n > 0) {
       // Descriptors of stage / Q / P buffer 0; buffer 1 is a fixed byte offset away.
       const uint64_t st_desc0 = sdesc_sw128(smem_u32(stage_mem), 16, 1024);
@@ -352,11 +357,12 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             const uint64_t bd = q_desc0 + (seg & 1) * (kQBytes >> 4);
             const uint32_t d = tmem_base + kColS + 64u * s;
 #pragma unroll
-            for (int k = 0; k < kChunks * 4; ++k) {
-              // K16 step k -> partial accumulator k % 4.  Descriptor offsets:
-              // +8192 bytes per 64-column chunk, +32 bytes per K16 step (>> 4).
-              umma_bf16(d + 16 * (k & 3), ad + (k >> 2) * (kChunkBytes >> 4) + (k & 3) * 2,
-                        bd + (k >> 2) * (kQChunkBytes >> 4) + (k & 3) * 2, kIdescS, k >= 4 ? 1u : 0u);
+            for (int c = 0; c < kChunks; ++c) {
+              // K16 step k = 4c + r -> partial accumulator r.  Descriptor
+              // offsets: +8192 bytes per 64-column chunk, +32 bytes per K16
+              // step (>> 4).
+              umma_bf16(d + 16 * r, ad + c * (kChunkBytes >> 4) + r * 2,
+                        bd + c * (kQChunkBytes >> 4) + r * 2, kIdescS, c > 0 ? 1u : 0u);
             }
             umma_commit(&s_full[s]);
             if (seg_end) umma_commit(&q_empty[seg & 1]);
@@ -376,13 +382,10 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             const uint32_t obuf = tmem_base + kColO + 64u * (seg & 1);
 #pragma unroll
             for (int kk = 0; kk < kRows / 16; ++kk) {
-#pragma unroll
-              for (int mb = 0; mb < 4; ++mb) {
-                // V^T block mb: chunks 2mb, 2mb+1; K16 step = 16 rows = 2048 bytes
-                umma_bf16(obuf + 16 * mb,
-                          v_desc0 + s * (kStageBytes >> 4) + mb * (2 * kChunkBytes >> 4) + kk * (2048 >> 4),
-                          p_desc0 + s * (kPBytes >> 4) + kk * 2, kIdescO, (seg_start && kk == 0) ? 0u : 1u);
-              }
+              // V^T block r: chunks 2r, 2r+1; K16 step = 16 rows = 2048 bytes
+              umma_bf16(obuf + 16 * r,
+                        v_desc0 + s * (kStageBytes >> 4) + r * (2 * kChunkBytes >> 4) + kk * (2048 >> 4),
+                        p_desc0 + s * (kPBytes >> 4) + kk * 2, kIdescO, (seg_start && kk == 0) ? 0u : 1u);
             }
             umma_commit(&kv_empty[s]);
             umma_commit(&p_empty[s]);
@@ -404,8 +407,8 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
           }
         }
       }
-      umma_commit(drain);
-      mbar_drain(drain, 0);
+      umma_commit(&drain[r]);
+      mbar_drain(&drain[r], 0);
     }
   } else {
     // ------------------------------------------------------ softmax warps
@@ -593,7 +596,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kMmaWarp0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
