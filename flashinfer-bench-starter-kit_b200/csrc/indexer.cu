@@ -568,9 +568,8 @@ __device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int m) {
 
 // Descending sort of the 2048 unique keys in buf (tmp: 2048 more slots).
 // Each warp sorts 64 keys in registers (bitonic, 2 per lane); then five
-// merge-path levels merge runs of 64, 128, ... 1024 keys, every thread
-// producing 2 outputs per level with one 16-byte store.  Every thread of the
-// block must call it; returns the buffer that holds the result.
+// merge-path levels merge runs of 64, 128, ... 1024 keys.  Every thread of
+// the block must call it; returns the buffer that holds the result.
 __device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp) {
   const int t = threadIdx.x;
   const int lane = t & 31;
@@ -597,27 +596,36 @@ __device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp) {
   uint64_t* dst = tmp;
   *reinterpret_cast<ulonglong2*>(src + 2 * t) = make_ulonglong2(x0, x1);
   __syncthreads();
+  // Merge levels: 256 threads, 8 consecutive outputs each, so one binary
+  // search (merge-path split) per 8 outputs instead of per 2.
 #pragma unroll 1
   for (int R = 64; R < kTopK; R <<= 1) {
-    const int o = 2 * t;                 // first of this thread's two outputs
-    const int pair = o / (2 * R);
-    const int d = o - pair * 2 * R;      // diagonal inside the pair
-    const uint64_t* A = src + pair * 2 * R;
-    const uint64_t* B = A + R;
-    // number of A keys among the d largest of A u B
-    int lo = d > R ? d - R : 0, hi = d < R ? d : R;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (A[mid] > B[d - 1 - mid]) lo = mid + 1; else hi = mid;
+    if (t < kTopK / 8) {
+      const int o = 8 * t;                 // first of this thread's eight outputs
+      const int pair = o / (2 * R);
+      const int d = o - pair * 2 * R;      // diagonal inside the pair
+      const uint64_t* A = src + pair * 2 * R;
+      const uint64_t* B = A + R;
+      // number of A keys among the d largest of A u B
+      int lo = d > R ? d - R : 0, hi = d < R ? d : R;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (A[mid] > B[d - 1 - mid]) lo = mid + 1; else hi = mid;
+      }
+      int ia = lo, ib = d - lo;
+      uint64_t a = ia < R ? A[ia] : 0ull, bb = ib < R ? B[ib] : 0ull;
+      uint64_t r[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const bool take_a = ib >= R || (ia < R && a > bb);
+        r[k] = take_a ? a : bb;
+        if (take_a) { ++ia; a = ia < R ? A[ia] : 0ull; }
+        else { ++ib; bb = ib < R ? B[ib] : 0ull; }
+      }
+#pragma unroll
+      for (int k = 0; k < 8; k += 2)
+        *reinterpret_cast<ulonglong2*>(dst + o + k) = make_ulonglong2(r[k], r[k + 1]);
     }
-    int ia = lo, ib = d - lo;
-    const bool take_a = ib >= R || (ia < R && A[ia] > B[ib]);
-    const uint64_t r0 = take_a ? A[ia] : B[ib];
-    ia += take_a ? 1 : 0;
-    ib += take_a ? 0 : 1;
-    const bool take_a2 = ib >= R || (ia < R && A[ia] > B[ib]);
-    const uint64_t r1 = take_a2 ? A[ia] : B[ib];
-    *reinterpret_cast<ulonglong2*>(dst + o) = make_ulonglong2(r0, r1);
     __syncthreads();
     uint64_t* sw = src; src = dst; dst = sw;
   }
@@ -658,12 +666,16 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     int need = K - res[1];
     int count = res[2];
     // One pass over the scores: every key whose top 11 bits are >= bin1 goes
-    // to this warp's private staging area (warp-uniform counter in a
-    // register: no shared atomics).  key >= bin1 << 21 is one float compare
-    // against the float with that key (NaN ranks highest).  Each thread
-    // loads 4 float4 (16 scores) per round.
+    // to this warp's private staging area.  key >= bin1 << 21 is one
+    // unordered float compare against the float with that key (NaN ranks
+    // highest).  Each thread loads 4 float4 (16 scores) per round and packs
+    // its verdicts into a 16-bit mask; a warp scan of the mask popcounts
+    // places the (rare) winners, which are re-read by index.
     const uint32_t tkey = bin1 << 21;
-    const float thr = __uint_as_float((tkey & 0x80000000u) ? (tkey & 0x7FFFFFFFu) : ~tkey);
+    float thr = __uint_as_float((tkey & 0x80000000u) ? (tkey & 0x7FFFFFFFu) : ~tkey);
+    // Bins above +inf hold only NaN (every NaN has the top key): stage NaN
+    // and +inf then; the refinement below drops the +inf keys again.
+    if (thr != thr) thr = INFINITY;
     const float4* row4 = reinterpret_cast<const float4*>(row);
     const int L4 = (L + 3) >> 2;                         // float4s covering [0, L)
     uint64_t* mine = stage + warp * kStageCap;
@@ -675,21 +687,41 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
         const int q = q0 + u * kSelThreads + tid;
         v[u] = q < L4 ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+      uint32_t msk = 0;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int q = q0 + u * kSelThreads + tid;
-        const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        msk |= (!(v[u].x < thr) ? 1u : 0u) << (4 * u);
+        msk |= (!(v[u].y < thr) ? 2u : 0u) << (4 * u);
+        msk |= (!(v[u].z < thr) ? 4u : 0u) << (4 * u);
+        msk |= (!(v[u].w < thr) ? 8u : 0u) << (4 * u);
+      }
+      if (q0 + 4 * kSelThreads > L4 - 1) {  // last round: drop positions >= L
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int i = 4 * q + c;
-          const bool pred = i < L && (e[c] >= thr || e[c] != e[c]);
-          const unsigned m = __ballot_sync(0xffffffffu, pred);
-          if (m) {
-            const int pos = wcount + __popc(m & ((1u << lane) - 1u));
-            if (pred && pos < kStageCap) mine[pos] = composite(e[c], i);
-            wcount += __popc(m);
-          }
+        for (int u = 0; u < 4; ++u) {
+          const int i0 = 4 * (q0 + u * kSelThreads + tid);
+          const int nv = L - i0;
+          const uint32_t keep = nv >= 4 ? 0xFu : (nv > 0 ? (1u << nv) - 1u : 0u);
+          msk &= ~(0xFu << (4 * u)) | (keep << (4 * u));
         }
+      }
+      const int cnt = __popc(msk);
+      int incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int wtot = __shfl_sync(0xffffffffu, incl, 31);
+      if (wtot) {
+        int pos = wcount + incl - cnt;
+        while (msk) {
+          const int bit = __ffs(msk) - 1;
+          msk &= msk - 1;
+          const int i = 4 * (q0 + (bit >> 2) * kSelThreads + tid) + (bit & 3);
+          if (pos < kStageCap) mine[pos] = composite(row[i], i);
+          ++pos;
+        }
+        wcount += wtot;
       }
     }
     if (lane == 0) {
@@ -709,11 +741,11 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
       for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
       __syncthreads();
       if (staged) {
-        for (int i = tid; i < kStageTotal; i += kSelThreads) {
-          if ((i & (kStageCap - 1)) < wcnt[i / kStageCap]) {
-            const uint64_t c = stage[i];
-            if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
-          }
+        const uint64_t* area = stage + warp * kStageCap;
+        const int avail = wcnt[warp];
+        for (int j = lane; j < avail; j += 32) {
+          const uint64_t c = area[j];
+          if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
         }
       } else {
         for (int i = tid; i < L; i += kSelThreads) {
