@@ -10,14 +10,12 @@
 //   T x 32 tiles of 64 selected rows; CTA c takes the contiguous slice
 //   [c*U/G, (c+1)*U/G) ("stream-K"), so every SM streams the same number of
 //   rows whatever T is.  Roles:
-//     warps 4-11 producers: read the tile's 64 slot ids (one tile ahead) and
-//                TMA tile::gather4 the rows' ckv (8 x 128-byte chunks) and
-//                kpe (1 chunk) into a 2-deep ring with 128-byte swizzle.  A
-//                thread issues gather4 ops at a fixed rate (about 70 cycles
-//                each), so the 144 ops of a tile are split over 8 warps:
-//                warp 4+w takes row half w >> 2 and chunks w&3, (w&3)+4 and,
-//                for w&3 == 0, the kpe chunk.  Warp 4 also loads q_nope / q_pe
-//                by 2-D TMA per token.
+//     warps 4-11 producers, two groups of four, one per stage of a 2-deep
+//                ring: read the tile's 64 slot ids (one tile ahead) and copy
+//                the rows' ckv (8 x 128-byte chunks) and kpe (1 chunk) with
+//                16-byte cp.async into the 128-byte-swizzled K-major layout.
+//                The group owning a token's first tile also loads q_nope /
+//                q_pe by 2-D TMA.
 //     warps 12-15 MMA issuers (tcgen05, bf16, fp32 accumulators in TMEM),
 //                each issuing logits and PV in whatever order their inputs
 //                become ready:
@@ -35,7 +33,8 @@
 //                so O in TMEM is rarely touched), P^T written as bf16.
 //   A token fully covered by one CTA is normalised and written directly;
 //   otherwise each covering CTA writes an (O, m, l) partial and bumps a
-//   per-token counter; the last one to arrive merges them:
+//   per-token counter; the last one to arrive merges them once its own
+//   tiles are done, with all of its threads:
 //   lse = log2 sum_i l_i 2^(m_i - M) + M, out = sum_i O_i 2^(m_i - M) / l.
 //   The counters are cleared by an async memset at the start of every call.
 #include <cuda_bf16.h>
@@ -72,6 +71,9 @@ constexpr uint32_t kColO = 0;    // O^T buffers at [0,64) and [64,128): 4 blocks
 constexpr uint32_t kColS = 128;  // S^T buffers at [128,192) and [192,256): 4 partial sums x 16 heads
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: factor 256
 constexpr int kMaxTokens = (1 << 30) / (kTopK / kRows) / kHeads;
+// Most partial records a token can have (its 32 tiles meet at most 33 CTA
+// slices); the merge scratch holds two [kMaxParts][16] float arrays.
+constexpr int kMaxParts = 64;
 
 // bf16 x bf16 -> f32.  Logits: A = K rows (K-major), B = Q (K-major), M64 N16.
 constexpr uint32_t kIdescS = idesc_make(1, 1, false, false, 64, 16);
@@ -86,9 +88,13 @@ constexpr int kOffBar = kOffSx + kHeads * kRows * 4; // 192512
 constexpr int kOffMisc = kOffBar + 256;
 constexpr int kSmemBytes = 1024 + kOffMisc + 256;
 static_assert((18 + kMmaWarps) * 8 <= 256, "barrier area");
+static_assert(kOffSx == kOffP + 2 * kPBytes && 2 * kPBytes + kHeads * kRows * 4 >= 2 * kMaxParts * kHeads * 4,
+              "merge scratch: the P and Sx buffers, contiguous");
 
 struct Params {
   const int32_t* indices;
+  const uint8_t* ckv;      // [num_slots][512] bf16
+  const uint8_t* kpe;      // [num_slots][64] bf16
   __nv_bfloat16* out;
   float* lse;
   float* part_o;   // [records][16][512]
@@ -123,56 +129,85 @@ __device__ __forceinline__ int parts_of(int t, int64_t total, int grid) {
   return hi - lo + 1;
 }
 
-// Merges the (O, m, l) partials of token t; run by the 128 softmax threads of
-// the CTA that wrote the last partial.  scratch: >= 16 * 33 floats of smem.
-__device__ void merge_token(const Params& p, int t, int64_t total, int grid, int e, float* scratch) {
+// Merges the (O, m, l) partials of token t.  Run by all kThreads threads of
+// the CTA that wrote the token's last partial, after its own work is done;
+// sm: 2 * kMaxParts * 16 floats of shared memory.  The per-part (m, l) loads
+// are all in flight together, and each thread keeps four parts' 16 output
+// columns in flight per round, so a token costs about ceil(parts / 4) + 1
+// L2 round trips:
+//   lse = log2 sum_i l_i 2^(m_i - M) + M,  out = sum_i O_i 2^(m_i - M) / l.
+__device__ void merge_token(const Params& p, int t, int64_t total, int grid, float* sm) {
+  const int tid = threadIdx.x;
   int c_lo, c_hi;
   covering_ctas(t, total, grid, c_lo, c_hi);
   const int nparts = c_hi - c_lo + 1;
-  // Per-head weights w[i][h] = 2^(m_i - M) / l, and lse.
-  if (e < kHeads) {
-    float M = -INFINITY;
-    for (int c = c_lo; c <= c_hi; ++c) {
-      const int64_t rec = static_cast<int64_t>(c) * p.kmax +
-                          (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
-      M = fmaxf(M, __ldcg(p.part_ml + rec * 2 * kHeads + 2 * e));
-    }
-    float l = 0.f;
-    for (int c = c_lo; c <= c_hi; ++c) {
-      const int64_t rec = static_cast<int64_t>(c) * p.kmax +
-                          (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
-      const float mi = __ldcg(p.part_ml + rec * 2 * kHeads + 2 * e);
-      const float li = __ldcg(p.part_ml + rec * 2 * kHeads + 2 * e + 1);
-      const float w = mi == -INFINITY ? 0.f : exp2f(mi - M);
-      scratch[(c - c_lo) * kHeads + e] = w;
-      l += li * w;
-    }
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    for (int i = 0; i < nparts; ++i) scratch[i * kHeads + e] *= inv;
-    p.lse[static_cast<int64_t>(t) * kHeads + e] = l > 0.f ? M + log2f(l) : -INFINITY;
+  if (nparts > kMaxParts) {  // cannot happen for grids of <= 2^20 CTAs; never read past sm
+    if (tid == 0) atomicOr(p.status, DSA_DEV_BAD_INDEX);
+    return;
   }
-  named_barrier_sync(1, 128);
-  // Thread e combines 64 consecutive outputs: head e/8, columns 64*(e%8)...
-  const int h = e >> 3;
-  const int c0 = (e & 7) * 64;
-  float acc[64];
-#pragma unroll
-  for (int k = 0; k < 64; ++k) acc[k] = 0.f;
-  for (int c = c_lo; c <= c_hi; ++c) {
+  float* mw = sm;                      // m_i[h], then the weight 2^(m_i - M) / l
+  float* lv = sm + kMaxParts * kHeads; // l_i[h]
+  for (int idx = tid; idx < nparts * kHeads; idx += kThreads) {
+    const int c = c_lo + (idx >> 4), hh = idx & 15;
     const int64_t rec = static_cast<int64_t>(c) * p.kmax +
                         (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
-    const float w = scratch[(c - c_lo) * kHeads + h];
-    const float4* src = reinterpret_cast<const float4*>(p.part_o + (rec * kHeads + h) * kCkv + c0);
+    mw[idx] = __ldcg(p.part_ml + rec * 2 * kHeads + 2 * hh);
+    lv[idx] = __ldcg(p.part_ml + rec * 2 * kHeads + 2 * hh + 1);
+  }
+  __syncthreads();
+  if (tid < kHeads) {
+    float M = -INFINITY;
+    for (int i = 0; i < nparts; ++i) M = fmaxf(M, mw[i * kHeads + tid]);
+    float l = 0.f;
+    for (int i = 0; i < nparts; ++i) {
+      const float mi = mw[i * kHeads + tid];
+      const float w = mi == -INFINITY ? 0.f : exp2f(mi - M);
+      l += lv[i * kHeads + tid] * w;
+      mw[i * kHeads + tid] = w;
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    for (int i = 0; i < nparts; ++i) mw[i * kHeads + tid] *= inv;
+    p.lse[static_cast<int64_t>(t) * kHeads + tid] = l > 0.f ? M + log2f(l) : -INFINITY;
+  }
+  __syncthreads();
+  // Thread -> head tid / 32, 16 consecutive columns: a warp reads 2 KB
+  // contiguous per part.
+  const int h = tid >> 5;
+  const int c0 = (tid & 31) * 16;
+  float acc[16];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const float4 v = __ldcg(src + k);
-      acc[4 * k] += v.x * w; acc[4 * k + 1] += v.y * w;
-      acc[4 * k + 2] += v.z * w; acc[4 * k + 3] += v.w * w;
+  for (int k = 0; k < 16; ++k) acc[k] = 0.f;
+  for (int i0 = 0; i0 < nparts; i0 += 4) {
+    float4 v[4][4];
+    float w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = i0 + k;
+      w[k] = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[k][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < nparts) {
+        const int c = c_lo + i;
+        const int64_t rec = static_cast<int64_t>(c) * p.kmax +
+                            (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
+        w[k] = mw[i * kHeads + h];
+        const float4* src = reinterpret_cast<const float4*>(p.part_o + (rec * kHeads + h) * kCkv + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[k][q] = __ldcg(src + q);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[4 * q] += v[k][q].x * w[k]; acc[4 * q + 1] += v[k][q].y * w[k];
+        acc[4 * q + 2] += v[k][q].z * w[k]; acc[4 * q + 3] += v[k][q].w * w[k];
+      }
     }
   }
   __nv_bfloat16* out = p.out + (static_cast<int64_t>(t) * kHeads + h) * kCkv + c0;
 #pragma unroll
-  for (int k = 0; k < 64; k += 8) {
+  for (int k = 0; k < 16; k += 8) {
     __nv_bfloat162 a0 = __floats2bfloat162_rn(acc[k], acc[k + 1]);
     __nv_bfloat162 a1 = __floats2bfloat162_rn(acc[k + 2], acc[k + 3]);
     __nv_bfloat162 a2 = __floats2bfloat162_rn(acc[k + 4], acc[k + 5]);
@@ -182,6 +217,7 @@ __device__ void merge_token(const Params& p, int t, int64_t total, int grid, int
     pk.z = *reinterpret_cast<uint32_t*>(&a2); pk.w = *reinterpret_cast<uint32_t*>(&a3);
     *reinterpret_cast<uint4*>(out + k) = pk;
   }
+  __syncthreads();  // sm is reused by the next merge
 }
 
 __device__ __forceinline__ int sanitize_slot(int v, int64_t num_slots, unsigned int* status) {
@@ -218,6 +254,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + kOffMisc + 4);
   int* rescale_flag = reinterpret_cast<int*>(smem + kOffMisc + 8);
+  int* merge_list = reinterpret_cast<int*>(smem + kOffMisc + 12);  // count, then <= 2 tokens
   float* alpha_smem = reinterpret_cast<float*>(smem + kOffMisc + 64);   // 16
   float* ml_smem = reinterpret_cast<float*>(smem + kOffMisc + 128);     // 16 x (m, l)
 
@@ -227,7 +264,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
 
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], kProdWarps); mbar_init(&kv_empty[s], kMmaWarps);
+      mbar_init(&kv_full[s], 32 * kProdWarps / 2); mbar_init(&kv_empty[s], kMmaWarps);
       mbar_init(&q_full[s], 1);  mbar_init(&q_empty[s], kMmaWarps);
       mbar_init(&s_full[s], kMmaWarps);  mbar_init(&s_empty[s], 128);
       mbar_init(&p_full[s], 1);  mbar_init(&p_empty[s], kMmaWarps);
@@ -236,6 +273,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     for (int w = 0; w < kMmaWarps; ++w) mbar_init(&drain[w], 1);
     *abort_flag = 0;
     *rescale_flag = 0;
+    merge_list[0] = 0;
     fence_mbar_init();
   }
   if (warp == kProdWarp0 && lane == 0) {
@@ -257,33 +295,52 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
 
   if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
     // ------------------------------------------------------ producer warps
-    // Warp 4+w gathers rows 32*(w>>2) .. +31 (lanes 0-7: 4 rows each) of
-    // chunks w&3, (w&3)+4 and, for w&3 == 0, 8 (the kpe chunk).
+    // Two groups of four warps; group g fills stage g with the rows of tiles
+    // i = g, g+2, ... by 16-byte cp.async straight into the 128-byte-swizzled
+    // K-major layout the MMAs read (piece j of row r lands at
+    // r*128 + ((j ^ (r & 7)) << 4) of its chunk).  Thread (warp wl of the
+    // group, lane l) copies piece l & 7 of rows 16*wl + 4*q + (l >> 3),
+    // q = 0..3, in all 9 chunks: 36 copies, each warp instruction moving
+    // four 128-byte row pieces.  These are ordinary load/store-unit
+    // instructions, so a tile's copies are issued in a few hundred cycles
+    // (a thread hands TMA gather4 ops over only every ~100 cycles).  The
+    // thread then waits for its copies, makes them visible to the tensor
+    // core's async proxy and arrives on the stage's barrier.  The warp with
+    // wl == 0 of the group that owns a token segment's first tile also
+    // loads that token's q_nope / q_pe by 2-D TMA.
     const int w = warp - kProdWarp0;
-    const int half = w >> 2;
-    const int c0 = w & 3;
-    const int nchunks = c0 == 0 ? 3 : 2;
+    const int g = w >> 2;
+    const int wl = w & 3;
+    const int j = lane & 7;
+    const int rsub = lane >> 3;
     const uint64_t policy = make_policy_evict_first();
-    int nq = 0, i = 0;
-    auto load_idx = [&](int j) {
-      int v = 0;
-      if (j < n) {
-        const int64_t u = u0 + j;
-        v = __ldg(p.indices + (u / kTilesPerTok) * kTopK + (u % kTilesPerTok) * kRows + 32 * half + lane);
+    const uint32_t st_s = smem_u32(stage_mem + g * kStageBytes);
+    auto load_idx = [&](int i, int (&v)[4]) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[q] = 0;
+      if (i < n) {
+        const int64_t u = u0 + i;
+        const int32_t* r = p.indices + (u / kTilesPerTok) * kTopK + (u % kTilesPerTok) * kRows + 16 * wl + rsub;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = __ldg(r + 4 * q);
       }
-      return v;
     };
-    int v = load_idx(0);
-    for (; i < n; ++i) {
+    int v[4];
+    load_idx(g, v);
+    int qseg[2] = {-1, -1};  // segments whose Q this warp loaded (last two)
+    int i = g;
+    for (; i < n; i += 2) {
       const int64_t u = u0 + i;
       const int t = static_cast<int>(u / kTilesPerTok);
       const int tile = static_cast<int>(u % kTilesPerTok);
-      const int nv = load_idx(i + 1);  // next tile's slot ids, in flight meanwhile
-      if (w == 0 && (i == 0 || tile == 0)) {
-        const int slot = nq & 1;
+      int nv[4];
+      load_idx(i + 2, nv);  // this group's next tile's slot ids, in flight meanwhile
+      if (wl == 0 && (i == 0 || tile == 0)) {
+        const int seg = t - t_first;
+        const int slot = seg & 1;
         int ok = 1;
         if (lane == 0) {
-          ok = mbar_wait(&q_empty[slot], ((nq >> 1) & 1) ^ 1, wctx);
+          ok = mbar_wait(&q_empty[slot], ((seg >> 1) & 1) ^ 1, wctx);
           if (ok) {
             mbar_arrive_expect_tx(&q_full[slot], kQBytes);
             uint8_t* q = q_mem + slot * kQBytes;
@@ -293,43 +350,38 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
           }
         }
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-        ++nq;
+        qseg[0] = qseg[1];
+        qseg[1] = seg;
       }
-      const int s = i & 1;
-      const int rv = sanitize_slot(v, p.num_slots, p.status);
-      int ok = 1;
-      if (lane == 0) {
-        ok = mbar_wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, wctx);
-        if (ok) mbar_arrive_expect_tx(&kv_full[s], nchunks * 8 * 512);
+      const int s = g;
+      if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, wctx))) break;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int row = 16 * wl + 4 * q + rsub;
+        const int64_t slotid = sanitize_slot(v[q], p.num_slots, p.status);
+        const uint8_t* ck = p.ckv + slotid * (kCkv * 2) + 16 * j;
+        const uint32_t dst = st_s + row * 128 + ((j ^ (row & 7)) << 4);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) cp_async16(dst + c * kChunkBytes, ck + 128 * c, policy);
+        cp_async16(dst + 8 * kChunkBytes, p.kpe + slotid * (kKpe * 2) + 16 * j, policy);
       }
-      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-      const int src = 4 * (lane & 7);
-      const int r0 = __shfl_sync(0xffffffffu, rv, src);
-      const int r1 = __shfl_sync(0xffffffffu, rv, src + 1);
-      const int r2 = __shfl_sync(0xffffffffu, rv, src + 2);
-      const int r3 = __shfl_sync(0xffffffffu, rv, src + 3);
-      if (lane < 8) {
-        uint8_t* dst = stage_mem + s * kStageBytes + (8 * half + lane) * 512;
-        tma_gather4(dst + c0 * kChunkBytes, &ckv_map, &kv_full[s], c0 * 64, r0, r1, r2, r3, policy);
-        tma_gather4(dst + (c0 + 4) * kChunkBytes, &ckv_map, &kv_full[s], (c0 + 4) * 64, r0, r1, r2, r3,
-                    policy);
-        if (c0 == 0)
-          tma_gather4(dst + 8 * kChunkBytes, &kpe_map, &kv_full[s], 0, r0, r1, r2, r3, policy);
-      }
-      __syncwarp();
-      v = nv;
+      cp_async_wait_all();
+      fence_proxy_async_smem();
+      mbar_arrive(&kv_full[s]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[q] = nv[q];
     }
-    if (lane == 0) {  // let in-flight copies land before the CTA can exit
-      for (int k = (i > 2 ? i - 2 : 0); k < i; ++k) mbar_drain(&kv_full[k & 1], (k >> 1) & 1);
-      if (w == 0)
-        for (int k = (nq > 2 ? nq - 2 : 0); k < nq; ++k) mbar_drain(&q_full[k & 1], (k >> 1) & 1);
+    cp_async_wait_all();  // copies of an aborted tile land before the CTA can exit
+    if (lane == 0) {
+      for (int k = 0; k < 2; ++k)
+        if (qseg[k] >= 0) mbar_drain(&q_full[qseg[k] & 1], (qseg[k] >> 1) & 1);
     }
   } else if (warp >= kMmaWarp0) {
     // ------------------------------------------------------ MMA issuers
     // Logits of tile i need its gathered rows, its token's Q and a free S
     // buffer; PV of tile i needs P(i) (and, at a segment start, a drained O
-    // buffer).  Both are polled and issued as soon as ready, so PV(i) never
-    // waits behind the next tile's gather.  Warp 12+r issues the logits K16
+    // buffer).  Both are polled and issued as soon as ready (PV first), so
+    // PV(i) never waits behind the next tile's gather or logits.  Warp 12+r issues the logits K16
     // steps k = r (mod 4) (partial accumulator r) and the PV of V^T block r.
     const int r = warp - kMmaWarp0;
     if (lane == 0 && n > 0) {
@@ -342,6 +394,30 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
       unsigned long long t_idle = 0;
       while (np < n) {
         bool progressed = false;
+        // PV first: it frees the K/V stage the gather of tile np + 2 waits for.
+        if (np < nl) {
+          const int64_t u = u0 + np;
+          const int tile = static_cast<int>(u % kTilesPerTok);
+          const int seg = static_cast<int>(u / kTilesPerTok) - t_first;
+          const bool seg_start = (np == 0 || tile == 0);
+          const int s = np & 1;
+          if (mbar_test(&p_full[s], (np >> 1) & 1) &&
+              (!seg_start || mbar_test(&o_empty[seg & 1], ((seg >> 1) & 1) ^ 1))) {
+            tc_fence_after();
+            const uint32_t obuf = tmem_base + kColO + 64u * (seg & 1);
+#pragma unroll
+            for (int kk = 0; kk < kRows / 16; ++kk) {
+              // V^T block r: chunks 2r, 2r+1; K16 step = 16 rows = 2048 bytes
+              umma_bf16(obuf + 16 * r,
+                        v_desc0 + s * (kStageBytes >> 4) + r * (2 * kChunkBytes >> 4) + kk * (2048 >> 4),
+                        p_desc0 + s * (kPBytes >> 4) + kk * 2, kIdescO, (seg_start && kk == 0) ? 0u : 1u);
+            }
+            umma_commit(&kv_empty[s]);
+            umma_commit(&p_empty[s]);
+            ++np;
+            progressed = true;
+          }
+        }
         if (nl < n) {
           const int64_t u = u0 + nl;
           const int tile = static_cast<int>(u % kTilesPerTok);
@@ -367,29 +443,6 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             umma_commit(&s_full[s]);
             if (seg_end) umma_commit(&q_empty[seg & 1]);
             ++nl;
-            progressed = true;
-          }
-        }
-        if (np < nl) {
-          const int64_t u = u0 + np;
-          const int tile = static_cast<int>(u % kTilesPerTok);
-          const int seg = static_cast<int>(u / kTilesPerTok) - t_first;
-          const bool seg_start = (np == 0 || tile == 0);
-          const int s = np & 1;
-          if (mbar_test(&p_full[s], (np >> 1) & 1) &&
-              (!seg_start || mbar_test(&o_empty[seg & 1], ((seg >> 1) & 1) ^ 1))) {
-            tc_fence_after();
-            const uint32_t obuf = tmem_base + kColO + 64u * (seg & 1);
-#pragma unroll
-            for (int kk = 0; kk < kRows / 16; ++kk) {
-              // V^T block r: chunks 2r, 2r+1; K16 step = 16 rows = 2048 bytes
-              umma_bf16(obuf + 16 * r,
-                        v_desc0 + s * (kStageBytes >> 4) + r * (2 * kChunkBytes >> 4) + kk * (2048 >> 4),
-                        p_desc0 + s * (kPBytes >> 4) + kk * 2, kIdescO, (seg_start && kk == 0) ? 0u : 1u);
-            }
-            umma_commit(&kv_empty[s]);
-            umma_commit(&p_empty[s]);
-            ++np;
             progressed = true;
           }
         }
@@ -584,10 +637,10 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
           const bool last = *rescale_flag == 2;
           named_barrier_sync(1, 128);
           if (e == 0) *rescale_flag = 0;
-          if (last) {
-            __threadfence();
-            merge_token(p, t, total, gridDim.x, e, sx);
-          }
+          // Only a CTA's first and last segments can be partial, so it merges
+          // at most two tokens; it does so once all of its roles are done,
+          // with every thread of the CTA.
+          if (last && e == 0) merge_list[1 + merge_list[0]++] = t;
         }
         named_barrier_sync(1, 128);  // ml_smem / sx are rewritten by the next segment
       }
@@ -599,6 +652,12 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   if (warp == kMmaWarp0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+  const int nmerge = merge_list[0];
+  if (nmerge > 0) {
+    __threadfence();  // the other CTAs' partials, published before their counter bumps
+    float* merge_sm = reinterpret_cast<float*>(p_mem);  // P and Sx, free now
+    for (int k = 0; k < nmerge && k < 2; ++k) merge_token(p, merge_list[1 + k], total, gridDim.x, merge_sm);
   }
 }
 
@@ -689,6 +748,8 @@ extern "C" int dsa_attention_run(const void* q_nope, const void* q_pe, const voi
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   attn::Params prm;
   prm.indices = sparse_indices;
+  prm.ckv = static_cast<const uint8_t*>(ckv_cache);
+  prm.kpe = static_cast<const uint8_t*>(kpe_cache);
   prm.out = static_cast<__nv_bfloat16*>(output);
   prm.lse = lse;
   prm.part_o = reinterpret_cast<float*>(ws + kWorkspaceHeader);
