@@ -32,10 +32,11 @@
 //                max is only moved when a tile exceeds it by more than 8,
 //                so O in TMEM is rarely touched), P^T written as bf16.
 //   A token fully covered by one CTA is normalised and written directly;
-//   otherwise each covering CTA writes an (O, m, l) partial and bumps a
-//   per-token counter; the last one to arrive merges them once its own
-//   tiles are done, with all of its threads:
-//   lse = log2 sum_i l_i 2^(m_i - M) + M, out = sum_i O_i 2^(m_i - M) / l.
+//   otherwise each covering CTA writes a partial (O / l in bf16, m, l) and
+//   bumps a per-token counter; the last one to arrive merges them once its
+//   own tiles are done, with all of its threads:
+//   lse = log2 L + M with L = sum_i l_i 2^(m_i - M),
+//   out = sum_i (O_i / l_i) l_i 2^(m_i - M) / L.
 //   The counters are cleared by an async memset at the start of every call.
 #include <cuda_bf16.h>
 
@@ -72,8 +73,9 @@ constexpr uint32_t kColS = 128;  // S^T buffers at [128,192) and [192,256): 4 pa
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: factor 256
 constexpr int kMaxTokens = (1 << 30) / (kTopK / kRows) / kHeads;
 // Most partial records a token can have (its 32 tiles meet at most 33 CTA
-// slices); the merge scratch holds two [kMaxParts][16] float arrays.
-constexpr int kMaxParts = 64;
+// slices); the merge scratch holds two [kMaxParts][16] float arrays and the
+// parts' record indices.
+constexpr int kMaxParts = 48;
 
 // bf16 x bf16 -> f32.  Logits: A = K rows (K-major), B = Q (K-major), M64 N16.
 constexpr uint32_t kIdescS = idesc_make(1, 1, false, false, 64, 16);
@@ -88,7 +90,8 @@ constexpr int kOffBar = kOffSx + kHeads * kRows * 4; // 192512
 constexpr int kOffMisc = kOffBar + 256;
 constexpr int kSmemBytes = 1024 + kOffMisc + 256;
 static_assert((18 + kMmaWarps) * 8 <= 256, "barrier area");
-static_assert(kOffSx == kOffP + 2 * kPBytes && 2 * kPBytes + kHeads * kRows * 4 >= 2 * kMaxParts * kHeads * 4,
+static_assert(kOffSx == kOffP + 2 * kPBytes &&
+                  2 * kPBytes + kHeads * kRows * 4 >= 2 * kMaxParts * kHeads * 4 + kMaxParts * 8,
               "merge scratch: the P and Sx buffers, contiguous");
 
 struct Params {
@@ -97,8 +100,8 @@ struct Params {
   const uint8_t* kpe;      // [num_slots][64] bf16
   __nv_bfloat16* out;
   float* lse;
-  float* part_o;   // [records][16][512]
-  float* part_ml;  // [records][16][2]
+  __nv_bfloat16* part_o;  // [records][16][512]: the part's O / l
+  float* part_ml;         // [records][16][2]: the part's (m, l)
   int* tok_count;  // [num_tokens] partials written so far (cleared at every call)
   unsigned int* status;
   int64_t num_slots;
@@ -108,19 +111,24 @@ struct Params {
 };
 
 // Which tokens / records a CTA covers, shared by both kernels.
+// floor(total * c / grid) in double precision: total * c < 2^53 is exact and
+// a non-integral quotient lies at least 1/grid from an integer, far above the
+// rounding error, so the floor is exact -- and much cheaper on the GPU than
+// a 64-bit integer division.
 __host__ __device__ inline int64_t unit_start(int64_t total, int c, int grid) {
-  return total * c / grid;
+  return static_cast<int64_t>(static_cast<double>(total) * c / grid);
 }
 
 // CTAs c whose unit range [start(c), start(c+1)) meets token t's units.
 __device__ __forceinline__ void covering_ctas(int t, int64_t total, int grid, int& c_lo, int& c_hi) {
+  // The CTA holding unit x is the largest c with start(c) <= x, i.e.
+  // floor(((x + 1) * grid - 1) / total) (every CTA holds >= 1 unit); exact
+  // in double precision like unit_start.
   const int64_t a = static_cast<int64_t>(t) * kTilesPerTok, z = a + kTilesPerTok;
-  int c = static_cast<int>(a * grid / total);
-  while (c > 0 && unit_start(total, c, grid) > a) --c;
-  while (unit_start(total, c + 1, grid) <= a) ++c;
-  c_lo = c;
-  while (c + 1 < grid && unit_start(total, c + 1, grid) < z) ++c;
-  c_hi = c;
+  const double dt = static_cast<double>(total);
+  c_lo = static_cast<int>(static_cast<double>((a + 1) * grid - 1) / dt);
+  c_hi = static_cast<int>(static_cast<double>(z * grid - 1) / dt);
+  if (c_hi > grid - 1) c_hi = grid - 1;
 }
 
 __device__ __forceinline__ int parts_of(int t, int64_t total, int grid) {
@@ -135,7 +143,8 @@ __device__ __forceinline__ int parts_of(int t, int64_t total, int grid) {
 // are all in flight together, and each thread keeps four parts' 16 output
 // columns in flight per round, so a token costs about ceil(parts / 4) + 1
 // L2 round trips:
-//   lse = log2 sum_i l_i 2^(m_i - M) + M,  out = sum_i O_i 2^(m_i - M) / l.
+//   lse = log2 L + M with L = sum_i l_i 2^(m_i - M), out = sum_i (O_i / l_i) l_i 2^(m_i - M) / L
+// (parts are stored normalised, O_i / l_i, in bf16).
 __device__ void merge_token(const Params& p, int t, int64_t total, int grid, float* sm) {
   const int tid = threadIdx.x;
   int c_lo, c_hi;
@@ -147,10 +156,16 @@ __device__ void merge_token(const Params& p, int t, int64_t total, int grid, flo
   }
   float* mw = sm;                      // m_i[h], then the weight 2^(m_i - M) / l
   float* lv = sm + kMaxParts * kHeads; // l_i[h]
+  int64_t* recs = reinterpret_cast<int64_t*>(sm + 2 * kMaxParts * kHeads);
+  if (tid < nparts) {
+    const int c = c_lo + tid;
+    recs[tid] = static_cast<int64_t>(c) * p.kmax +
+                (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
+  }
+  __syncthreads();
   for (int idx = tid; idx < nparts * kHeads; idx += kThreads) {
-    const int c = c_lo + (idx >> 4), hh = idx & 15;
-    const int64_t rec = static_cast<int64_t>(c) * p.kmax +
-                        (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
+    const int hh = idx & 15;
+    const int64_t rec = recs[idx >> 4];
     mw[idx] = __ldcg(p.part_ml + rec * 2 * kHeads + 2 * hh);
     lv[idx] = __ldcg(p.part_ml + rec * 2 * kHeads + 2 * hh + 1);
   }
@@ -161,9 +176,9 @@ __device__ void merge_token(const Params& p, int t, int64_t total, int grid, flo
     float l = 0.f;
     for (int i = 0; i < nparts; ++i) {
       const float mi = mw[i * kHeads + tid];
-      const float w = mi == -INFINITY ? 0.f : exp2f(mi - M);
-      l += lv[i * kHeads + tid] * w;
-      mw[i * kHeads + tid] = w;
+      const float w = mi == -INFINITY ? 0.f : lv[i * kHeads + tid] * exp2f(mi - M);
+      l += w;
+      mw[i * kHeads + tid] = w;  // the parts hold O_i / l_i
     }
     const float inv = l > 0.f ? 1.f / l : 0.f;
     for (int i = 0; i < nparts; ++i) mw[i * kHeads + tid] *= inv;
@@ -178,30 +193,32 @@ __device__ void merge_token(const Params& p, int t, int64_t total, int grid, flo
 #pragma unroll
   for (int k = 0; k < 16; ++k) acc[k] = 0.f;
   for (int i0 = 0; i0 < nparts; i0 += 4) {
-    float4 v[4][4];
+    uint4 v[4][2];
     float w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int i = i0 + k;
       w[k] = 0.f;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) v[k][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      v[k][0] = v[k][1] = make_uint4(0u, 0u, 0u, 0u);
       if (i < nparts) {
-        const int c = c_lo + i;
-        const int64_t rec = static_cast<int64_t>(c) * p.kmax +
-                            (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
+        const int64_t rec = recs[i];
         w[k] = mw[i * kHeads + h];
-        const float4* src = reinterpret_cast<const float4*>(p.part_o + (rec * kHeads + h) * kCkv + c0);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) v[k][q] = __ldcg(src + q);
+        const uint4* src = reinterpret_cast<const uint4*>(p.part_o + (rec * kHeads + h) * kCkv + c0);
+        v[k][0] = __ldcg(src);
+        v[k][1] = __ldcg(src + 1);
       }
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        acc[4 * q] += v[k][q].x * w[k]; acc[4 * q + 1] += v[k][q].y * w[k];
-        acc[4 * q + 2] += v[k][q].z * w[k]; acc[4 * q + 3] += v[k][q].w * w[k];
+      for (int q = 0; q < 2; ++q) {
+        const uint32_t wd[4] = {v[k][q].x, v[k][q].y, v[k][q].z, v[k][q].w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wd[r]));
+          acc[8 * q + 2 * r] += f.x * w[k];
+          acc[8 * q + 2 * r + 1] += f.y * w[k];
+        }
       }
     }
   }
@@ -616,11 +633,16 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
           }
         } else {
           const int64_t rec = static_cast<int64_t>(blockIdx.x) * p.kmax + (t - t_first);
-          float* po = p.part_o + rec * kHeads * kCkv;
+          __nv_bfloat16* po = p.part_o + rec * kHeads * kCkv;
+          // The part is stored normalised (O / l, |value| <= max |v|) in
+          // bf16: half the bytes for the merging CTA to read.
 #pragma unroll
-          for (int hh = 0; hh < kHeads; ++hh)
+          for (int hh = 0; hh < kHeads; ++hh) {
+            const float l = ml_smem[2 * hh + 1];
+            const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
-            for (int mb = 0; mb < 4; ++mb) po[hh * kCkv + 128 * mb + col] = o[mb][hh];
+            for (int mb = 0; mb < 4; ++mb) po[hh * kCkv + 128 * mb + col] = __float2bfloat16_rn(o[mb][hh] * inv);
+          }
           if (e < kHeads) {
             p.part_ml[rec * 2 * kHeads + 2 * e] = ml_smem[2 * e];
             p.part_ml[rec * 2 * kHeads + 2 * e + 1] = ml_smem[2 * e + 1];
@@ -676,7 +698,7 @@ inline size_t workspace_for(int num_tokens, int num_sms) {
   if (num_tokens <= 0) return kWorkspaceHeader;
   const int grid = grid_for(num_tokens, num_sms);
   const size_t recs = static_cast<size_t>(grid) * kmax_for(num_tokens, grid);
-  return kWorkspaceHeader + recs * kHeads * (kCkv + 2) * sizeof(float) +
+  return kWorkspaceHeader + recs * kHeads * (2 * sizeof(float) + kCkv * sizeof(__nv_bfloat16)) +
          sizeof(int) * static_cast<size_t>(num_tokens);
 }
 
@@ -752,9 +774,9 @@ extern "C" int dsa_attention_run(const void* q_nope, const void* q_pe, const voi
   prm.kpe = static_cast<const uint8_t*>(kpe_cache);
   prm.out = static_cast<__nv_bfloat16*>(output);
   prm.lse = lse;
-  prm.part_o = reinterpret_cast<float*>(ws + kWorkspaceHeader);
-  prm.part_ml = prm.part_o + recs * attn::kHeads * attn::kCkv;
-  prm.tok_count = reinterpret_cast<int*>(prm.part_ml + recs * attn::kHeads * 2);
+  prm.part_ml = reinterpret_cast<float*>(ws + kWorkspaceHeader);
+  prm.part_o = reinterpret_cast<__nv_bfloat16*>(prm.part_ml + recs * attn::kHeads * 2);
+  prm.tok_count = reinterpret_cast<int*>(prm.part_o + recs * attn::kHeads * attn::kCkv);
   prm.status = reinterpret_cast<unsigned int*>(ws);
   prm.num_slots = num_slots;
   prm.num_tokens = num_tokens;
