@@ -488,6 +488,7 @@ constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kTopK = DSA_TOPK;
 constexpr int kStageCap = 512;                        // staged keys per warp
+constexpr int kMergeOut = 4;                          // sort: outputs per thread per merge level
 constexpr int kStageTotal = kSelWarps * kStageCap;    // 16384
 constexpr size_t kSelSmem = sizeof(uint64_t) * (kTopK + kStageTotal) + sizeof(uint32_t) * kBins +
                             sizeof(int) * (32 + 8 + kSelWarps);
@@ -596,12 +597,12 @@ __device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp) {
   uint64_t* dst = tmp;
   *reinterpret_cast<ulonglong2*>(src + 2 * t) = make_ulonglong2(x0, x1);
   __syncthreads();
-  // Merge levels: 256 threads, 8 consecutive outputs each, so one binary
-  // search (merge-path split) per 8 outputs instead of per 2.
+  // Merge levels: kMergeOut consecutive outputs per thread, so one binary
+  // search (merge-path split) per kMergeOut outputs.
 #pragma unroll 1
   for (int R = 64; R < kTopK; R <<= 1) {
-    if (t < kTopK / 8) {
-      const int o = 8 * t;                 // first of this thread's eight outputs
+    if (t < kTopK / kMergeOut) {
+      const int o = kMergeOut * t;         // first of this thread's outputs
       const int pair = o / (2 * R);
       const int d = o - pair * 2 * R;      // diagonal inside the pair
       const uint64_t* A = src + pair * 2 * R;
@@ -614,16 +615,16 @@ __device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp) {
       }
       int ia = lo, ib = d - lo;
       uint64_t a = ia < R ? A[ia] : 0ull, bb = ib < R ? B[ib] : 0ull;
-      uint64_t r[8];
+      uint64_t r[kMergeOut];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < kMergeOut; ++k) {
         const bool take_a = ib >= R || (ia < R && a > bb);
         r[k] = take_a ? a : bb;
         if (take_a) { ++ia; a = ia < R ? A[ia] : 0ull; }
         else { ++ib; bb = ib < R ? B[ib] : 0ull; }
       }
 #pragma unroll
-      for (int k = 0; k < 8; k += 2)
+      for (int k = 0; k < kMergeOut; k += 2)
         *reinterpret_cast<ulonglong2*>(dst + o + k) = make_ulonglong2(r[k], r[k + 1]);
     }
     __syncthreads();
