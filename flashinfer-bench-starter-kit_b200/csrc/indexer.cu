@@ -681,12 +681,21 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     const int L4 = (L + 3) >> 2;                         // float4s covering [0, L)
     uint64_t* mine = stage + warp * kStageCap;
     int wcount = 0;
+    // Loads run one round ahead of the compares, so the L2 latency of round
+    // r + 1 overlaps the work on round r.
+    float4 nv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = u * kSelThreads + tid;
+      nv[u] = q < L4 ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     for (int q0 = 0; q0 < L4; q0 += 4 * kSelThreads) {
       float4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int q = q0 + u * kSelThreads + tid;
-        v[u] = q < L4 ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[u] = nv[u];
+        const int q = q0 + (4 + u) * kSelThreads + tid;
+        nv[u] = q < L4 ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       uint32_t msk = 0;
 #pragma unroll
@@ -768,18 +777,12 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
       const uint64_t* area = stage + warp * kStageCap;
       const int avail = wcnt[warp];
       int cnt = 0;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const int j = lane + 32 * k;
-        cnt += (j < avail && (area[j] & mask) >= prefix) ? 1 : 0;
-      }
+      for (int j = lane; j < avail; j += 32) cnt += (area[j] & mask) >= prefix ? 1 : 0;
       const int incl = block_scan_incl(cnt, warp_tot);
       int pos = incl - cnt;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const int j = lane + 32 * k;
+      for (int j = lane; j < avail; j += 32) {
         const uint64_t c = area[j];
-        if (j < avail && (c & mask) >= prefix) sel[pos++] = c;
+        if ((c & mask) >= prefix) sel[pos++] = c;
       }
     } else {
       const int Lr = (L + 31) & ~31;
