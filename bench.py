@@ -256,7 +256,7 @@ def main() -> int:
 
     import torch.distributed as dist
 
-    from dsa_b200 import pipeline, workloads
+    from dsa_b200 import pipeline, sharding, workloads
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -309,16 +309,8 @@ def main() -> int:
     barrier()
     ix_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / K
     at_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / K
-    stats = torch.tensor([ms_total, float(rank_bytes), float(len(lens))], dtype=torch.float64,
-                         device=dev)
-    if world > 1:
-        mx = stats.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = stats.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        ms_total, total_bytes, n_req = float(mx[0]), float(sm[1]), float(sm[2])
-    else:
-        total_bytes, n_req = float(rank_bytes), float(len(lens))
+    ms_total, total_bytes, n_req = sharding.reduce_step_stats(ms_total, float(rank_bytes),
+                                                              float(len(lens)), world)
     ms_step = ms_total / K
     value = total_bytes / (ms_step * 1e-3) / 1e9
 

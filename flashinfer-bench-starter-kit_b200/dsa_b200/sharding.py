@@ -34,3 +34,24 @@ def shard_imbalance(seq_lens: list, shards: list) -> float:
     loads = [sum(max(0, int(seq_lens[i])) for i in s) for s in shards]
     mean = sum(loads) / max(1, len(loads))
     return max(loads) / mean if mean > 0 else 1.0
+
+
+def reduce_step_stats(ms_total: float, rank_bytes: float, rank_requests: float, world: int) -> tuple:
+    """Whole-job step statistics from every rank's: time is the MAX over ranks
+    (the job is done when its slowest rank is), bytes and requests are SUMS.
+    Uses torch.distributed when world > 1 (NCCL on GPUs, gloo on CPU); every
+    rank must call it, in the same order as its other collectives."""
+    import torch
+
+    if world <= 1:
+        return float(ms_total), float(rank_bytes), float(rank_requests)
+    import torch.distributed as dist
+
+    backend = dist.get_backend()
+    dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+    stats = torch.tensor([ms_total, rank_bytes, rank_requests], dtype=torch.float64, device=dev)
+    mx = stats.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    sm = stats.clone()
+    dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    return float(mx[0]), float(sm[1]), float(sm[2])
