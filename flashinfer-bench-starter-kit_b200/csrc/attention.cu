@@ -163,6 +163,26 @@ __device__ void merge_token(const Params& p, int t, int64_t total, int grid, flo
                 (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
   }
   __syncthreads();
+  // Thread -> head tid / 32, 16 consecutive columns: a warp reads 2 KB
+  // contiguous per part.  The first four parts' columns and every part's
+  // (m, l) are requested together, so the weights below are computed while
+  // the column loads are in flight.
+  const int h = tid >> 5;
+  const int c0 = (tid & 31) * 16;
+  auto load4 = [&](int i0, uint4 (&v)[4][2]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[k][0] = v[k][1] = make_uint4(0u, 0u, 0u, 0u);
+      if (i0 + k < nparts) {
+        const uint4* src =
+            reinterpret_cast<const uint4*>(p.part_o + (recs[i0 + k] * kHeads + h) * kCkv + c0);
+        v[k][0] = __ldcg(src);
+        v[k][1] = __ldcg(src + 1);
+      }
+    }
+  };
+  uint4 v[4][2];
+  load4(0, v);
   for (int idx = tid; idx < nparts * kHeads; idx += kThreads) {
     const int hh = idx & 15;
     const int64_t rec = recs[idx >> 4];
@@ -185,39 +205,22 @@ __device__ void merge_token(const Params& p, int t, int64_t total, int grid, flo
     p.lse[static_cast<int64_t>(t) * kHeads + tid] = l > 0.f ? M + log2f(l) : -INFINITY;
   }
   __syncthreads();
-  // Thread -> head tid / 32, 16 consecutive columns: a warp reads 2 KB
-  // contiguous per part.
-  const int h = tid >> 5;
-  const int c0 = (tid & 31) * 16;
   float acc[16];
 #pragma unroll
   for (int k = 0; k < 16; ++k) acc[k] = 0.f;
   for (int i0 = 0; i0 < nparts; i0 += 4) {
-    uint4 v[4][2];
-    float w[4];
+    if (i0 > 0) load4(i0, v);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int i = i0 + k;
-      w[k] = 0.f;
-      v[k][0] = v[k][1] = make_uint4(0u, 0u, 0u, 0u);
-      if (i < nparts) {
-        const int64_t rec = recs[i];
-        w[k] = mw[i * kHeads + h];
-        const uint4* src = reinterpret_cast<const uint4*>(p.part_o + (rec * kHeads + h) * kCkv + c0);
-        v[k][0] = __ldcg(src);
-        v[k][1] = __ldcg(src + 1);
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
+      const float w = i0 + k < nparts ? mw[(i0 + k) * kHeads + h] : 0.f;
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         const uint32_t wd[4] = {v[k][q].x, v[k][q].y, v[k][q].z, v[k][q].w};
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
           const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wd[r]));
-          acc[8 * q + 2 * r] += f.x * w[k];
-          acc[8 * q + 2 * r + 1] += f.y * w[k];
+          acc[8 * q + 2 * r] += f.x * w;
+          acc[8 * q + 2 * r + 1] += f.y * w;
         }
       }
     }
@@ -234,7 +237,6 @@ __device__ void merge_token(const Params& p, int t, int64_t total, int grid, flo
     pk.z = *reinterpret_cast<uint32_t*>(&a2); pk.w = *reinterpret_cast<uint32_t*>(&a3);
     *reinterpret_cast<uint4*>(out + k) = pk;
   }
-  __syncthreads();  // sm is reused by the next merge
 }
 
 __device__ __forceinline__ int sanitize_slot(int v, int64_t num_slots, unsigned int* status) {
@@ -679,7 +681,10 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   if (nmerge > 0) {
     __threadfence();  // the other CTAs' partials, published before their counter bumps
     float* merge_sm = reinterpret_cast<float*>(p_mem);  // P and Sx, free now
-    for (int k = 0; k < nmerge && k < 2; ++k) merge_token(p, merge_list[1 + k], total, gridDim.x, merge_sm);
+    for (int k = 0; k < nmerge && k < 2; ++k) {
+      if (k > 0) __syncthreads();  // the merge scratch is reused
+      merge_token(p, merge_list[1 + k], total, gridDim.x, merge_sm);
+    }
   }
 }
 
