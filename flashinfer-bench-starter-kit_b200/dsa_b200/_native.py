@@ -33,6 +33,8 @@ SIGNATURES = {
                                               _P]),
     "dsa_indexer_run_noalloc": (ctypes.c_int, [_P, _P, ctypes.c_int64, _P, _P, _P, ctypes.c_int32,
                                                ctypes.c_int32, _P, _P]),
+    "dsa_index_cache_write": (ctypes.c_int, [_P, _P, ctypes.c_int32, _P, ctypes.c_int64,
+                                             ctypes.c_int32, _P, _P]),
 }
 
 _lib = None

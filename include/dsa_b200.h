@@ -165,6 +165,27 @@ DSA_API int dsa_indexer_run_noalloc(const void* q_index_fp8, const void* k_index
                                     int32_t batch, int32_t max_pages, int32_t* topk_indices,
                                     void* stream);
 
+/* Quantises new indexer keys into the paged FP8 K cache (the step before
+ * dsa_indexer_run in a serving loop).
+ *
+ *   k                  [num_tokens, 128] bf16, 8-byte aligned
+ *   slot_mapping       [num_tokens] int64 global slot ids (page*64 + token);
+ *                      negative = padding, skipped
+ *   k_index_cache_fp8  num_pages pages of 8448 bytes (the layout
+ *                      dsa_indexer_run reads), 16-byte aligned
+ *   ue8m0              non-zero: round each scale up to a power of two
+ *   status             optional device word (NULL = none): DSA_DEV_BAD_INDEX
+ *                      is OR-ed in for a slot >= num_pages*64 (not written)
+ *
+ * Per token: scale = max(1e-4, max|k|)/448 (ue8m0: 2^ceil(log2 scale)),
+ * fp8 = e4m3(k/scale) round-to-nearest-even, stored at the token's row and
+ * scale slot.  The reference only defines the page layout
+ * (dsa_indexer/solution/triton/kernel.py:80,120-124); the arithmetic is the
+ * published vLLM indexer cache writer (indexer_k_quant_and_cache). */
+DSA_API int dsa_index_cache_write(const void* k, const int64_t* slot_mapping, int32_t num_tokens,
+                                  void* k_index_cache_fp8, int64_t num_pages, int32_t ue8m0,
+                                  uint32_t* status, void* stream);
+
 /* Copies the sticky device status word of `workspace` to *status_out
  * (synchronising `stream`), and zeroes it when `clear` is non-zero.
  * No counterpart in the reference, which has no error channel
