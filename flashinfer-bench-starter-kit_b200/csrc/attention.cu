@@ -274,6 +274,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   int* abort_flag = reinterpret_cast<int*>(smem + kOffMisc + 4);
   int* rescale_flag = reinterpret_cast<int*>(smem + kOffMisc + 8);
   int* merge_list = reinterpret_cast<int*>(smem + kOffMisc + 12);  // count, then <= 2 tokens
+  int* q_last = reinterpret_cast<int*>(smem + kOffMisc + 32);      // last segment loaded per Q slot
   float* alpha_smem = reinterpret_cast<float*>(smem + kOffMisc + 64);   // 16
   float* ml_smem = reinterpret_cast<float*>(smem + kOffMisc + 128);     // 16 x (m, l)
 
@@ -293,6 +294,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     *abort_flag = 0;
     *rescale_flag = 0;
     merge_list[0] = 0;
+    q_last[0] = q_last[1] = -1;
     fence_mbar_init();
   }
   if (warp == kProdWarp0 && lane == 0) {
@@ -346,7 +348,6 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     };
     int v[4];
     load_idx(g, v);
-    int qseg[2] = {-1, -1};  // segments whose Q this warp loaded (last two)
     int i = g;
     for (; i < n; i += 2) {
       const int64_t u = u0 + i;
@@ -366,11 +367,10 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             for (int c = 0; c < 8; ++c)
               tma_load_2d(q + c * kQChunkBytes, &qn_map, &q_full[slot], c * 64, t * kHeads);
             tma_load_2d(q + 8 * kQChunkBytes, &qp_map, &q_full[slot], 0, t * kHeads);
+            atomicMax(&q_last[slot], seg);
           }
         }
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-        qseg[0] = qseg[1];
-        qseg[1] = seg;
       }
       const int s = g;
       if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, wctx))) break;
@@ -391,10 +391,6 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
       for (int q = 0; q < 4; ++q) v[q] = nv[q];
     }
     cp_async_wait_all();  // copies of an aborted tile land before the CTA can exit
-    if (lane == 0) {
-      for (int k = 0; k < 2; ++k)
-        if (qseg[k] >= 0) mbar_drain(&q_full[qseg[k] & 1], (qseg[k] >> 1) & 1);
-    }
   } else if (warp >= kMmaWarp0) {
     // ------------------------------------------------------ MMA issuers
     // Logits of tile i need its gathered rows, its token's Q and a free S
@@ -480,7 +476,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
         }
       }
       umma_commit(&drain[r]);
-      mbar_drain(&drain[r], 0);
+      mbar_drain(&drain[r], 0, p.status);
     }
   } else {
     // ------------------------------------------------------ softmax warps
@@ -676,6 +672,15 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   if (warp == kMmaWarp0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (warp == kProdWarp0 && lane == 0) {
+    // A Q load still in flight (only after an abort) must land before exit.
+    // Only the last load of each slot can be: loading segment s + 2 waits
+    // until segment s was consumed.  Its phase parity is unambiguous because
+    // nothing reloads the slot afterwards; an older segment's parity would
+    // read as pending again once the slot has been refilled twice.
+    for (int k = 0; k < 2; ++k)
+      if (q_last[k] >= 0) mbar_drain(&q_full[k], (q_last[k] >> 1) & 1, p.status);
   }
   const int nmerge = merge_list[0];
   if (nmerge > 0) {

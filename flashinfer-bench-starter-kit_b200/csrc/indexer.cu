@@ -306,7 +306,7 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
     if (lane == 0) {  // let every copy this thread issued land before the CTA can exit
       for (int j = (m > 2 ? m - 2 : 0); j < m; ++j) {
         const int n = k + kProdWarps * j;
-        mbar_drain(&full[n % kStages], static_cast<uint32_t>((n / kStages) & 1));
+        mbar_drain(&full[n % kStages], static_cast<uint32_t>((n / kStages) & 1), p.status);
       }
     }
   } else if (warp >= kMmaWarp0) {
@@ -368,9 +368,9 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         }
       }
       umma_commit(&drain[parity]);
-      mbar_drain(&drain[parity], 0);
+      mbar_drain(&drain[parity], 0, p.status);
       if (parity == 0)  // a q load still in flight must land before exit
-        for (int j = (nq > 2 ? nq - 2 : 0); j < nq; ++j) mbar_drain(&qfull[j & 1], (j >> 1) & 1);
+        for (int j = (nq > 2 ? nq - 2 : 0); j < nq; ++j) mbar_drain(&qfull[j & 1], (j >> 1) & 1, p.status);
     }
     __syncwarp();
   } else {

@@ -112,11 +112,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
-// Short bounded wait used only while tearing down after an abort.
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+// Short bounded wait used while tearing down: lets an asynchronous copy or
+// MMA that may still be in flight complete before the CTA exits.  In a run
+// without an abort the phase has completed already.  Giving up (100 ms)
+// raises DSA_DEV_WAIT_TIMEOUT, since it means the caller's parity bookkeeping
+// or the hardware is broken.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsigned int* status) {
   const unsigned long long t0 = global_timer_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - t0 > 100000000ull) return;  // 100 ms
+    if (global_timer_ns() - t0 > 100000000ull) {  // 100 ms
+      atomicOr(status, DSA_DEV_WAIT_TIMEOUT);
+      return;
+    }
   }
 }
 

@@ -106,6 +106,22 @@ def test_many_tokens(cuda_device, T):
     check(a, out, lse, tokens=list(range(0, T, max(1, T // 24))) + [T - 1])
 
 
+@pytest.mark.parametrize("T", [512, 1500])
+def test_many_segments_per_cta(cuda_device, T):
+    # 148 CTAs over T*32 tiles give every CTA 4+ token segments, so both
+    # Q slots are refilled at least twice; the teardown drains only the last
+    # load of each slot (an older one's phase parity would read as pending
+    # and the drain would run out, raising the wait-timeout status bit).
+    import time
+    a = workloads.make_attention_inputs(T, pool_pages=4096, seed=200 + T, device=cuda_device)
+    run_gpu(a)
+    t0 = time.perf_counter()
+    out, lse = run_gpu(a)
+    dt = time.perf_counter() - t0
+    check(a, out, lse, tokens=list(range(0, T, max(1, T // 24))) + [T - 1])
+    assert dt < 0.05, f"{T} tokens took {dt * 1e3:.1f} ms"
+
+
 def test_large_logits_rescale(cuda_device):
     # Scaled logits spanning many units of log2 force the lazy rescale path.
     a = workloads.make_attention_inputs(4, pool_pages=512, seed=17, device=cuda_device)
