@@ -488,7 +488,7 @@ constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kTopK = DSA_TOPK;
 constexpr int kStageCap = 512;                        // staged keys per warp
-constexpr int kMergeOut = 4;                          // sort: outputs per thread per merge level
+constexpr int kMergeOut = 4;                          // merge sort: outputs per thread per level
 constexpr int kStageTotal = kSelWarps * kStageCap;    // 16384
 constexpr size_t kSelSmem = sizeof(uint64_t) * (kTopK + kStageTotal) + sizeof(uint32_t) * kBins +
                             sizeof(int) * (32 + 8 + kSelWarps);
@@ -567,11 +567,11 @@ __device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int m) {
   return (static_cast<uint64_t>(hi) << 32) | lo;
 }
 
-// Descending sort of the 2048 unique keys in buf (tmp: 2048 more slots).
-// Each warp sorts 64 keys in registers (bitonic, 2 per lane); then five
+// Descending sort of the 2048 keys in buf (tmp: 2048 more slots), for any
+// key distribution.  Each warp sorts 64 keys in registers (bitonic, 2 per lane); then five
 // merge-path levels merge runs of 64, 128, ... 1024 keys.  Every thread of
 // the block must call it; returns the buffer that holds the result.
-__device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp) {
+__device__ uint64_t* sort_desc_2048_merge(uint64_t* buf, uint64_t* tmp) {
   const int t = threadIdx.x;
   const int lane = t & 31;
   uint64_t x0 = buf[2 * t], x1 = buf[2 * t + 1];
@@ -633,6 +633,83 @@ __device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp) {
   return src;
 }
 
+// Descending sort of the 2048 keys in buf: the non-zero keys first (all
+// distinct: they carry their token index), then the zero padding keys of a
+// row shorter than 2048, which stay where the caller put them (at the end).
+// Bucket sort: an 11-bit digit of (key - min) over the keys' own range
+// [min, max] gives 2048 buckets in descending key order; shared-memory
+// atomics count them, a block scan places them, and each key's position
+// inside its bucket is the number of the bucket's keys greater than it.  If
+// the keys crowd into a few buckets (a bucket above kBucketCap keys), the
+// merge sort above runs instead.  tmp: 2048 keys; cnt: 2048 counters;
+// scratch: 64 keys; flag: one int, zero on entry.  Every thread of the block
+// must call it; returns the buffer that holds the result.
+constexpr int kBucketCap = 48;
+
+__device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp, uint32_t* cnt, int* warp_tot,
+                                    uint64_t* scratch, int* flag) {
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int warp = t >> 5;
+  const uint64_t x0 = buf[2 * t], x1 = buf[2 * t + 1];
+  uint64_t mx = x0 > x1 ? x0 : x1;
+  uint64_t mn = (x0 ? x0 : ~0ull) < (x1 ? x1 : ~0ull) ? (x0 ? x0 : ~0ull) : (x1 ? x1 : ~0ull);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t a = shfl_xor64(mx, o), c = shfl_xor64(mn, o);
+    mx = a > mx ? a : mx;
+    mn = c < mn ? c : mn;
+  }
+  if (lane == 0) { scratch[warp] = mx; scratch[32 + warp] = mn; }
+  cnt[t] = 0;
+  cnt[t + 1024] = 0;
+  __syncthreads();
+  mx = scratch[lane];
+  mn = scratch[32 + lane];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t a = shfl_xor64(mx, o), c = shfl_xor64(mn, o);
+    mx = a > mx ? a : mx;
+    mn = c < mn ? c : mn;
+  }
+  if (mx == 0) return buf;  // no keys at all
+  const uint64_t span = mx - mn;
+  const int shift = span < 2048 ? 0 : 64 - __clzll(static_cast<long long>(span)) - 11;
+  const bool v0 = x0 != 0, v1 = x1 != 0;
+  const int b0 = 2047 - static_cast<int>((x0 - mn) >> shift);
+  const int b1 = 2047 - static_cast<int>((x1 - mn) >> shift);
+  const int s0 = v0 ? static_cast<int>(atomicAdd(&cnt[b0], 1u)) : 0;
+  const int s1 = v1 ? static_cast<int>(atomicAdd(&cnt[b1], 1u)) : 0;
+  __syncthreads();
+  // Thread t owns buckets 2t, 2t + 1: counts -> exclusive starts.
+  const int c0 = static_cast<int>(cnt[2 * t]), c1 = static_cast<int>(cnt[2 * t + 1]);
+  if (c0 > kBucketCap || c1 > kBucketCap) atomicOr(flag, 1);
+  const int incl = block_scan_incl(c0 + c1, warp_tot);  // its barriers order the reads above
+  cnt[2 * t] = incl - c0 - c1;
+  cnt[2 * t + 1] = incl - c1;
+  __syncthreads();
+  if (*flag) return sort_desc_2048_merge(buf, tmp);
+  const int nvalid = warp_tot[31];
+  if (v0) tmp[cnt[b0] + s0] = x0;
+  if (v1) tmp[cnt[b1] + s1] = x1;
+  __syncthreads();
+  // Rank inside the bucket; the zero keys at buf[nvalid..] are not touched.
+  if (v0) {
+    const int st = cnt[b0], en = b0 < 2047 ? static_cast<int>(cnt[b0 + 1]) : nvalid;
+    int r = 0;
+    for (int j = st; j < en; ++j) r += tmp[j] > x0 ? 1 : 0;
+    buf[st + r] = x0;
+  }
+  if (v1) {
+    const int st = cnt[b1], en = b1 < 2047 ? static_cast<int>(cnt[b1 + 1]) : nvalid;
+    int r = 0;
+    for (int j = st; j < en; ++j) r += tmp[j] > x1 ? 1 : 0;
+    buf[st + r] = x1;
+  }
+  __syncthreads();
+  return buf;
+}
+
 __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const SelectParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint64_t* sel = reinterpret_cast<uint64_t*>(smem_raw);
@@ -655,7 +732,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
 
   // The histogram the score kernel accumulated for this request.
   for (int i = tid; i < kBins; i += kSelThreads) hist[i] = ghist[i];
-  if (tid == 0) { res[3] = 0; res[4] = 0; }
+  if (tid == 0) { res[3] = 0; res[4] = 0; res[5] = 0; }
   __syncthreads();
 
   if (L <= kTopK) {
@@ -795,7 +872,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     __syncthreads();
   }
 
-  const uint64_t* sorted = sort_desc_2048(sel, stage);
+  const uint64_t* sorted = sort_desc_2048(sel, stage, hist, warp_tot, stage + kTopK, &res[5]);
 
   int32_t* out = p.out + static_cast<int64_t>(b) * kTopK;
   const int32_t* bt = p.block_table + static_cast<int64_t>(b) * p.max_pages;

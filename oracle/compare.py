@@ -5,7 +5,10 @@ Indexer: outputs are compared as sets of global slot ids per request, plus the
 a swap is accepted only when the two tokens' oracle scores are within the
 fp32 reordering bound of each other (``oracle.indexer.score_error_bound``),
 i.e. when a different fp32 accumulation order could flip them.  Swaps are
-counted and returned so tests and the bench can report them.
+counted and returned so tests and the bench can report them.  The order is
+checked too (the reference returns torch.topk's sorted order): in a row that
+is not identical to the oracle's, every output must score at least the next
+one's oracle score minus the two tokens' rounding bounds.
 
 Attention: the contest harness rule -- an element fails only if
 ``abs_err > atol`` AND ``rel_err > rtol`` -- with atol = rtol = 1e-2 for the
@@ -29,6 +32,7 @@ class TopkReport:
     exact_rows: int = 0            # identical row, order included
     swaps: int = 0                 # slots selected by only one side
     max_swap_gap: float = 0.0      # largest |score gap| of an accepted swap
+    order_violations: int = 0      # adjacent outputs out of score order
     problems: list = field(default_factory=list)
 
 
@@ -64,8 +68,6 @@ def compare_topk(got: torch.Tensor, ref: torch.Tensor, scores: list, bounds: lis
             rep.problems.append(f"row {b}: duplicate slots")
             continue
         only_g, only_r = gs - rs, rs - gs
-        if not only_g:
-            continue  # same set, different order of (near-)equal scores
         inv = _slot_to_token(bt[b], L, num_pages)
         sc = scores[b].numpy().astype(np.float64)
         eb = bounds[b].numpy().astype(np.float64)
@@ -74,12 +76,24 @@ def compare_topk(got: torch.Tensor, ref: torch.Tensor, scores: list, bounds: lis
             t = inv[slot // _ix.PAGE_SIZE]
             return -1 if t < 0 else int(t * _ix.PAGE_SIZE + slot % _ix.PAGE_SIZE)
 
-        tg = [tok(s) for s in only_g]
-        tr = [tok(s) for s in only_r]
-        if min(tg) < 0 or max(tg) >= L:
+        tall = np.array([tok(s) for s in g[:kk]], dtype=np.int64)
+        if kk and (tall.min() < 0 or tall.max() >= L):
             rep.ok = False
             rep.problems.append(f"row {b}: slot outside the request's pages")
             continue
+        s_all, e_all = sc[tall], eb[tall]
+        bad = np.nonzero(s_all[1:] - s_all[:-1] > e_all[1:] + e_all[:-1])[0]
+        if bad.size:
+            rep.ok = False
+            rep.order_violations += int(bad.size)
+            i = int(bad[0])
+            rep.problems.append(f"row {b}: output {i + 1} (score {s_all[i + 1]:.7g}) ranks below "
+                                f"output {i} (score {s_all[i]:.7g})")
+            continue
+        if not only_g:
+            continue  # same set, different order of (near-)equal scores
+        tg = [tok(s) for s in only_g]
+        tr = [tok(s) for s in only_r]
         # every GPU-only token must be within rounding of every ref-only token
         worst_ref = min(tr, key=lambda t: sc[t])
         best_got = max(tg, key=lambda t: sc[t])

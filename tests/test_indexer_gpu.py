@@ -94,6 +94,19 @@ def test_all_equal_scores_break_ties_by_index(cuda_device):
         assert torch.equal(got, want), L
 
 
+def test_outlier_scores_keep_sorted_order(cuda_device):
+    # Scales 10^4 times larger on one page give a few scores far above the
+    # rest: the select's bucket sort then sees the other keys crowd into a few
+    # buckets and sorts with its merge-sort path instead.
+    ix = workloads.make_indexer_inputs([8192, 8192], pool_pages=300, seed=41, device=cuda_device)
+    kc = ix.k_index_cache_fp8.view(torch.uint8).reshape(ix.num_pages, -1)
+    page = int(ix.block_table[0, 0])
+    kc[page, 64 * 128:].view(torch.float32).mul_(1e4)
+    got = run_gpu(ix)
+    rep = oracle_check(ix, got)
+    assert rep.order_violations == 0
+
+
 def test_repeated_page_ties(cuda_device):
     # Every page of the request is the same physical page: 64 distinct
     # scores, each repeated L/64 times -> ties resolved by token index.

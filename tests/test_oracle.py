@@ -121,6 +121,22 @@ def test_compare_topk_rejects_a_planted_wrong_index():
     assert not rep.ok
 
 
+def test_compare_topk_rejects_a_planted_wrong_order():
+    q, kc, w, sl, bt, _, _ = _load_indexer_fixture()
+    ref, scores = oix.indexer_reference(q, kc, w, sl, bt)
+    kc_u8 = kc.view(torch.uint8).reshape(-1)
+    bounds = [oix.score_error_bound(q[b], kc_u8, w[b], int(sl[b]), bt[b].long())
+              for b in range(q.shape[0])]
+    # Same set, but the best and the 100th outputs of row 0 trade places.
+    bad = ref.clone()
+    bad[0, 0], bad[0, 99] = ref[0, 99].item(), ref[0, 0].item()
+    rep = compare.compare_topk(bad, ref, scores, bounds, sl, bt, kc.shape[0])
+    assert not rep.ok and rep.order_violations > 0
+    # Exactly equal scores may come in either order only when bounds allow:
+    # the oracle's own output passes untouched.
+    assert compare.compare_topk(ref, ref, scores, bounds, sl, bt, kc.shape[0]).ok
+
+
 def test_harness_close_rule():
     ref = torch.tensor([1.0, 100.0, -math.inf])
     assert compare.harness_close(torch.tensor([1.005, 100.5, -math.inf]), ref, 0.01, 0.01).ok
