@@ -636,48 +636,39 @@ __device__ uint64_t* sort_desc_2048_merge(uint64_t* buf, uint64_t* tmp) {
 // Descending sort of the 2048 keys in buf: the non-zero keys first (all
 // distinct: they carry their token index), then the zero padding keys of a
 // row shorter than 2048, which stay where the caller put them (at the end).
-// Bucket sort: an 11-bit digit of (key - min) over the keys' own range
-// [min, max] gives 2048 buckets in descending key order; shared-memory
-// atomics count them, a block scan places them, and each key's position
-// inside its bucket is the number of the bucket's keys greater than it.  If
+// Bucket sort: an 11-bit digit of the score word (key >> 32) over the
+// non-zero keys' own range of score words gives 2048 buckets in descending
+// key order; shared-memory atomics count them, a block scan places them, and
+// each key's position inside its bucket is the number of the bucket's keys
+// greater than it (full 64-bit compare, so equal scores order by token).  If
 // the keys crowd into a few buckets (a bucket above kBucketCap keys), the
 // merge sort above runs instead.  tmp: 2048 keys; cnt: 2048 counters;
-// scratch: 64 keys; flag: one int, zero on entry.  Every thread of the block
+// scratch: 64 words; flag: one int, zero on entry.  Every thread of the block
 // must call it; returns the buffer that holds the result.
 constexpr int kBucketCap = 48;
 
 __device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp, uint32_t* cnt, int* warp_tot,
-                                    uint64_t* scratch, int* flag) {
+                                    uint32_t* scratch, int* flag) {
   const int t = threadIdx.x;
   const int lane = t & 31;
   const int warp = t >> 5;
-  const uint64_t x0 = buf[2 * t], x1 = buf[2 * t + 1];
-  uint64_t mx = x0 > x1 ? x0 : x1;
-  uint64_t mn = (x0 ? x0 : ~0ull) < (x1 ? x1 : ~0ull) ? (x0 ? x0 : ~0ull) : (x1 ? x1 : ~0ull);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const uint64_t a = shfl_xor64(mx, o), c = shfl_xor64(mn, o);
-    mx = a > mx ? a : mx;
-    mn = c < mn ? c : mn;
-  }
+  const ulonglong2 xx = *reinterpret_cast<const ulonglong2*>(buf + 2 * t);
+  const uint64_t x0 = xx.x, x1 = xx.y;
+  const bool v0 = x0 != 0, v1 = x1 != 0;
+  const uint32_t h0 = static_cast<uint32_t>(x0 >> 32), h1 = static_cast<uint32_t>(x1 >> 32);
+  uint32_t mx = __reduce_max_sync(0xffffffffu, max(v0 ? h0 : 0u, v1 ? h1 : 0u));
+  uint32_t mn = __reduce_min_sync(0xffffffffu, min(v0 ? h0 : 0xFFFFFFFFu, v1 ? h1 : 0xFFFFFFFFu));
   if (lane == 0) { scratch[warp] = mx; scratch[32 + warp] = mn; }
   cnt[t] = 0;
   cnt[t + 1024] = 0;
   __syncthreads();
-  mx = scratch[lane];
-  mn = scratch[32 + lane];
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const uint64_t a = shfl_xor64(mx, o), c = shfl_xor64(mn, o);
-    mx = a > mx ? a : mx;
-    mn = c < mn ? c : mn;
-  }
-  if (mx == 0) return buf;  // no keys at all
-  const uint64_t span = mx - mn;
-  const int shift = span < 2048 ? 0 : 64 - __clzll(static_cast<long long>(span)) - 11;
-  const bool v0 = x0 != 0, v1 = x1 != 0;
-  const int b0 = 2047 - static_cast<int>((x0 - mn) >> shift);
-  const int b1 = 2047 - static_cast<int>((x1 - mn) >> shift);
+  mx = __reduce_max_sync(0xffffffffu, scratch[lane]);
+  mn = __reduce_min_sync(0xffffffffu, scratch[32 + lane]);
+  if (mx < mn) return buf;  // no non-zero keys
+  const uint32_t span = mx - mn;
+  const int shift = span < 2048 ? 0 : 32 - __clz(static_cast<int>(span)) - 11;
+  const int b0 = 2047 - static_cast<int>((h0 - mn) >> shift);
+  const int b1 = 2047 - static_cast<int>((h1 - mn) >> shift);
   const int s0 = v0 ? static_cast<int>(atomicAdd(&cnt[b0], 1u)) : 0;
   const int s1 = v1 ? static_cast<int>(atomicAdd(&cnt[b1], 1u)) : 0;
   __syncthreads();
@@ -748,7 +739,9 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     // unordered float compare against the float with that key (NaN ranks
     // highest).  Each thread loads 4 float4 (16 scores) per round and packs
     // its verdicts into a 16-bit mask; a warp scan of the mask popcounts
-    // places the (rare) winners, which are re-read by index.
+    // places the (rare) winners, whose token indices are staged; their
+    // scores are fetched after the pass with independent loads (a re-read
+    // inside the loop would serialise one L2 round trip per winner).
     const uint32_t tkey = bin1 << 21;
     float thr = __uint_as_float((tkey & 0x80000000u) ? (tkey & 0x7FFFFFFFu) : ~tkey);
     // Bins above +inf hold only NaN (every NaN has the top key): stage NaN
@@ -758,6 +751,9 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     const int L4 = (L + 3) >> 2;                         // float4s covering [0, L)
     uint64_t* mine = stage + warp * kStageCap;
     int wcount = 0;
+    // find_bin has read the first-level histogram; it is rebuilt below as
+    // the second-level one (next 11 bits of the boundary bin).
+    for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
     // Loads run one round ahead of the compares, so the L2 latency of round
     // r + 1 overlaps the work on round r.
     float4 nv[4];
@@ -805,7 +801,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
           const int bit = __ffs(msk) - 1;
           msk &= msk - 1;
           const int i = 4 * (q0 + (bit >> 2) * kSelThreads + tid) + (bit & 3);
-          if (pos < kStageCap) mine[pos] = composite(row[i], i);
+          if (pos < kStageCap) mine[pos] = static_cast<uint64_t>(i);
           ++pos;
         }
         wcount += wtot;
@@ -817,30 +813,56 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     }
     __syncthreads();
     const bool staged = res[3] == 0;
+    if (staged) {
+      // Scores of this warp's staged tokens, four independent loads in
+      // flight per lane; keys of the boundary bin count into the histogram
+      // of the first refinement pass.
+      const int avail = wcount;
+      for (int j0 = lane; j0 < avail; j0 += 128) {
+        int ti[4];
+        float sv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) ti[u] = j0 + 32 * u < avail ? static_cast<int>(mine[j0 + 32 * u]) : 0;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sv[u] = j0 + 32 * u < avail ? __ldg(row + ti[u]) : 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (j0 + 32 * u < avail) {
+            const uint64_t c = composite(sv[u], ti[u]);
+            mine[j0 + 32 * u] = c;
+            if (static_cast<uint32_t>(c >> 53) == bin1) atomicAdd(&hist[(c >> 42) & 0x7FF], 1u);
+          }
+        }
+      }
+      __syncthreads();
+    }
     uint64_t prefix = static_cast<uint64_t>(bin1) << 53;
     uint64_t mask = static_cast<uint64_t>(0x7FF) << 53;
-    // Refine the boundary: 11-bit digits of the remaining 53 key bits.
+    // Refine the boundary: 11-bit digits of the remaining 53 key bits.  With
+    // the keys staged, the first pass's histogram was built above.
     const int shifts[5] = {42, 31, 20, 9, 0};
     const int widths[5] = {11, 11, 11, 11, 9};
     for (int pass = 0; pass < 5 && count != need; ++pass) {
       const int sh = shifts[pass];
       const uint64_t dm = (static_cast<uint64_t>(1) << widths[pass]) - 1;
-      for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
-      __syncthreads();
-      if (staged) {
-        const uint64_t* area = stage + warp * kStageCap;
-        const int avail = wcnt[warp];
-        for (int j = lane; j < avail; j += 32) {
-          const uint64_t c = area[j];
-          if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
+      if (pass > 0 || !staged) {
+        for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
+        __syncthreads();
+        if (staged) {
+          const uint64_t* area = stage + warp * kStageCap;
+          const int avail = wcnt[warp];
+          for (int j = lane; j < avail; j += 32) {
+            const uint64_t c = area[j];
+            if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
+          }
+        } else {
+          for (int i = tid; i < L; i += kSelThreads) {
+            const uint64_t c = composite(row[i], i);
+            if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
+          }
         }
-      } else {
-        for (int i = tid; i < L; i += kSelThreads) {
-          const uint64_t c = composite(row[i], i);
-          if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
-        }
+        __syncthreads();
       }
-      __syncthreads();
       find_bin(hist, need, warp_tot, res);
       prefix |= static_cast<uint64_t>(res[0]) << sh;
       mask |= dm << sh;
@@ -872,7 +894,8 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     __syncthreads();
   }
 
-  const uint64_t* sorted = sort_desc_2048(sel, stage, hist, warp_tot, stage + kTopK, &res[5]);
+  const uint64_t* sorted =
+      sort_desc_2048(sel, stage, hist, warp_tot, reinterpret_cast<uint32_t*>(stage + kTopK), &res[5]);
 
   int32_t* out = p.out + static_cast<int64_t>(b) * kTopK;
   const int32_t* bt = p.block_table + static_cast<int64_t>(b) * p.max_pages;
