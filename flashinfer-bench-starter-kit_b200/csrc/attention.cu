@@ -102,7 +102,7 @@ struct Params {
   float* lse;
   __nv_bfloat16* part_o;  // [records][16][512]: the part's O / l
   float* part_ml;         // [records][16][2]: the part's (m, l)
-  int* tok_count;  // [num_tokens] partials written so far (cleared at every call)
+  int* tok_count;  // [num_tokens] partials written so far; zero between calls (the merging CTA resets it)
   unsigned int* status;
   int64_t num_slots;
   int num_tokens;
@@ -305,6 +305,9 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Launched programmatically after the indexer's select kernel: global
+  // memory is touched only once the previous grid has completed.
+  griddep_wait();
 
   const uint32_t tmem_base = *tmem_base_smem;
   const int64_t total = static_cast<int64_t>(p.num_tokens) * kTilesPerTok;
@@ -649,8 +652,13 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
           __threadfence();
           named_barrier_sync(1, 128);
           if (e == 0) {
+            const int parts = parts_of(t, total, gridDim.x);
             const int prev = atomicAdd(p.tok_count + t, 1);
-            const int last = prev == parts_of(t, total, gridDim.x) - 1;
+            const int last = prev == parts - 1;
+            // The last part leaves the counter at zero for the next call; a
+            // count already at `parts` means the workspace held a stale one.
+            if (last) p.tok_count[t] = 0;
+            if (prev >= parts) atomicOr(p.status, DSA_DEV_STALE_WORKSPACE);
             *rescale_flag = last ? 2 : 0;  // reuse the flag word as a broadcast
           }
           named_barrier_sync(1, 128);
@@ -786,7 +794,13 @@ extern "C" int dsa_attention_run(const void* q_nope, const void* q_pe, const voi
   prm.lse = lse;
   prm.part_ml = reinterpret_cast<float*>(ws + kWorkspaceHeader);
   prm.part_o = reinterpret_cast<__nv_bfloat16*>(prm.part_ml + recs * attn::kHeads * 2);
-  prm.tok_count = reinterpret_cast<int*>(prm.part_o + recs * attn::kHeads * attn::kCkv);
+  // The merge counters sit at the end of the buffer: every call leaves them
+  // at zero, and no call with another token count puts partial records
+  // there (records grow from the front, and workspace_for(T) >= records(T)
+  // + counters(T) with records(T) non-decreasing in T), so they need no
+  // clearing as long as every call passes the same workspace_bytes.
+  prm.tok_count = reinterpret_cast<int*>(
+      ws + ((workspace_bytes - sizeof(int) * static_cast<size_t>(num_tokens)) & ~static_cast<size_t>(3)));
   prm.status = reinterpret_cast<unsigned int*>(ws);
   prm.num_slots = num_slots;
   prm.num_tokens = num_tokens;
@@ -794,11 +808,9 @@ extern "C" int dsa_attention_run(const void* q_nope, const void* q_pe, const voi
   prm.scale_log2 = sm_scale * 1.4426950408889634f;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(prm.tok_count, 0, sizeof(int) * static_cast<size_t>(num_tokens), s) !=
-      cudaSuccess)
+  if (launch_programmatic(attn::attention_kernel, dim3(grid), dim3(attn::kThreads), attn::kSmemBytes,
+                          s, ckv_map, kpe_map, qn_map, qp_map, prm) != cudaSuccess)
     return DSA_ERR_CUDA;
-  attn::attention_kernel<<<grid, attn::kThreads, attn::kSmemBytes, s>>>(ckv_map, kpe_map, qn_map,
-                                                                       qp_map, prm);
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
   return DSA_OK;
 }

@@ -33,4 +33,24 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Launches `kernel` on `stream` with programmatic stream serialization, so
+// its CTAs may be scheduled while the previous kernel on the stream drains
+// (the kernel synchronises with griddep_wait() before touching global
+// memory).  Capturable into CUDA graphs.
+template <typename... Params, typename... Args>
+cudaError_t launch_programmatic(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                                cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 }  // namespace dsa

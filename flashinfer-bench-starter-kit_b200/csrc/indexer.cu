@@ -200,6 +200,9 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int max_len = p.max_pages * kPage;
+  // The select kernel may start launching now: it waits for this grid's
+  // completion before it reads anything.
+  griddep_launch_dependents();
 
   if (tid == 0) {
     // full: the owning producer warp's arrive.expect_tx.  accempty: the four
@@ -715,6 +718,10 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int max_len = p.max_pages * kPage;
+  // Launched programmatically after the score kernel: nothing in global
+  // memory is touched before that grid has completed.
+  griddep_wait();
+  griddep_launch_dependents();
   int L = __ldg(p.seq_lens + b);
   L = L < 0 ? 0 : (L > max_len ? max_len : L);  // the score kernel flags bad lengths
   const float* row = p.scores + static_cast<int64_t>(b) * p.score_stride;
@@ -996,7 +1003,9 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
   selp.out = topk_indices;
   selp.score_stride = sp.score_stride;
   selp.max_pages = max_pages;
-  ix::topk_select_kernel<<<batch, ix::kSelThreads, ix::kSelSmem, s>>>(selp);
+  if (launch_programmatic(ix::topk_select_kernel, dim3(batch), dim3(ix::kSelThreads), ix::kSelSmem,
+                          s, selp) != cudaSuccess)
+    return DSA_ERR_CUDA;
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
   return DSA_OK;
 }

@@ -29,6 +29,22 @@ __device__ __forceinline__ unsigned long long global_timer_ns() {
   return t;
 }
 
+// ------------------------------------------------- programmatic launch
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel on its stream is still running.  It must not touch
+// global memory before griddep_wait(), which returns once that kernel has
+// completed and its writes are visible; before it, only CTA-local set-up
+// (shared memory, mbarriers, TMEM allocation, tensor-map prefetch) is done.
+// griddep_launch_dependents() lets the next such kernel start launching.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

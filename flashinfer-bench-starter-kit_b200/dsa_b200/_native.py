@@ -17,6 +17,7 @@ DEV_BAD_SEQ_LEN = 0x1
 DEV_BAD_PAGE = 0x2
 DEV_BAD_INDEX = 0x4
 DEV_WAIT_TIMEOUT = 0x8
+DEV_STALE_WORKSPACE = 0x10
 
 # name -> (restype, argtypes); every symbol include/dsa_b200.h declares.
 _P = ctypes.c_void_p
@@ -79,4 +80,6 @@ def describe_device_status(bits: int) -> str:
         names.append("sparse index outside [-1, num_slots)")
     if bits & DEV_WAIT_TIMEOUT:
         names.append("a kernel pipeline wait timed out")
+    if bits & DEV_STALE_WORKSPACE:
+        names.append("a workspace merge counter was not zero on entry (zero-fill the workspace)")
     return ", ".join(names) if names else "ok"

@@ -61,6 +61,8 @@ extern "C" {
 #define DSA_DEV_BAD_PAGE      0x2u  /* block_table entry outside [0, num_pages) */
 #define DSA_DEV_BAD_INDEX     0x4u  /* sparse index outside [-1, num_slots)     */
 #define DSA_DEV_WAIT_TIMEOUT  0x8u  /* a bounded pipeline wait gave up          */
+#define DSA_DEV_STALE_WORKSPACE 0x10u /* a merge counter was not zero on entry:   */
+                                      /* zero-fill the workspace again            */
 
 /* Shape constants of the two contest definitions
  * dsa_topk_indexer_fp8_h64_d128_topk2048_ps64 and
@@ -111,12 +113,18 @@ DSA_API int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cache_f
 
 /* Bytes of device workspace dsa_attention_run needs for num_tokens queries
  * on this device: a 256-byte header, the split-softmax partial records and
- * one merge counter per token (cleared by the call with an async memset).
- * Zero-fill a workspace once before its first use so the status word in its
- * header starts clear. */
+ * one merge counter per token, placed at the end of the workspace.  Zero-fill
+ * a workspace once before its first use (status word and counters start at
+ * zero; every completed call leaves the counters at zero again) and pass the
+ * same workspace_bytes to every call on it.  After a call that raised
+ * DSA_DEV_WAIT_TIMEOUT, zero-fill it again (a stale counter is reported as
+ * DSA_DEV_STALE_WORKSPACE). */
 DSA_API size_t dsa_attention_workspace_bytes(int32_t num_tokens);
 
 /* Sparse MLA attention, one query token per row of sparse_indices.
+ * Launched with programmatic stream serialization: it may be scheduled while
+ * the previous kernel on `stream` drains, and touches global memory only
+ * after that kernel has completed.
  *
  *   q_nope          [num_tokens, 16, 512] bf16
  *   q_pe            [num_tokens, 16, 64]  bf16

@@ -11,6 +11,7 @@ import pytest
 import torch
 
 from dsa_b200 import DsaError, attention, workloads
+from dsa_b200 import workspace as ws_mod
 from oracle import attention as oatt
 from oracle import compare
 
@@ -120,6 +121,30 @@ def test_many_segments_per_cta(cuda_device, T):
     dt = time.perf_counter() - t0
     check(a, out, lse, tokens=list(range(0, T, max(1, T // 24))) + [T - 1])
     assert dt < 0.05, f"{T} tokens took {dt * 1e3:.1f} ms"
+
+
+def test_merge_counters_are_left_zero_and_stale_ones_reported(cuda_device):
+    # 64 tokens over the SM count: every token is split and merged.  Each
+    # call leaves its merge counters (at the end of the workspace) at zero;
+    # a counter planted non-zero is reported instead of silently skipping a
+    # merge.
+    T = 64
+    a = workloads.make_attention_inputs(T, pool_pages=2048, seed=43, device=cuda_device)
+    out, lse = run_gpu(a)
+    check(a, out, lse, tokens=[0, 31, 63])
+    dev = torch.device(cuda_device)
+    buf = ws_mod.get(dev, "attention", 0, torch.cuda.current_stream(dev).cuda_stream)
+    W = buf.numel()
+    off = (W - 4 * T) & ~3
+    assert int(buf[off:off + 4 * T].view(torch.int32).abs().sum()) == 0
+    buf[off:off + 4].view(torch.int32).fill_(1000)
+    try:
+        with pytest.raises(DsaError, match="merge counter"):
+            run_gpu(a)
+    finally:
+        buf.zero_()
+    out, lse = run_gpu(a)
+    check(a, out, lse, tokens=[0, 31, 63])
 
 
 def test_large_logits_rescale(cuda_device):
