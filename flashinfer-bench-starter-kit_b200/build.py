@@ -18,7 +18,7 @@ ROOT = pathlib.Path(__file__).resolve().parent
 REPO = ROOT.parent
 CSRC = ROOT / "csrc"
 OUT = ROOT / "dsa_b200" / "libdsa_b200.so"
-SOURCES = ["capi.cu", "indexer.cu", "attention.cu", "noalloc.cu", "cache_write.cu"]
+SOURCES = ["capi.cu", "indexer.cu", "attention.cu", "noalloc.cu", "cache_write.cu", "prefill.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

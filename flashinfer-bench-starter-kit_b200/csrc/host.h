@@ -33,6 +33,15 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Launches the indexer's top-2048 select over `rows` score rows (one CTA
+// each, programmatically after the kernel that wrote the scores): row b
+// reads scores[b], hist[b], seq_lens[b] and block-table row row_req[b]
+// (row_req == nullptr: row b; a negative entry yields an all -1 row).
+int launch_topk_select(const float* scores, const unsigned int* hist, const int32_t* seq_lens,
+                       const int32_t* block_table, const int32_t* row_req, int32_t* out, int rows,
+                       int score_stride, int max_pages, unsigned int* status, const DeviceInfo& info,
+                       cudaStream_t s);
+
 // Launches `kernel` on `stream` with programmatic stream serialization, so
 // its CTAs may be scheduled while the previous kernel on the stream drains
 // (the kernel synchronises with griddep_wait() before touching global

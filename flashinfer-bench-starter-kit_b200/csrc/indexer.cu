@@ -498,6 +498,8 @@ constexpr size_t kSelSmem = sizeof(uint64_t) * (kTopK + kStageTotal) + sizeof(ui
 
 struct SelectParams {
   const float* scores;
+  const int32_t* row_req;  // block-table row of each score row; nullptr: the row itself
+  unsigned int* status;
   const unsigned int* hist;
   const int32_t* seq_lens;
   const int32_t* block_table;
@@ -724,6 +726,8 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
   griddep_launch_dependents();
   int L = __ldg(p.seq_lens + b);
   L = L < 0 ? 0 : (L > max_len ? max_len : L);  // the score kernel flags bad lengths
+  const int bt_row = p.row_req ? __ldg(p.row_req + b) : b;
+  if (bt_row < 0) L = 0;  // a row outside every request: all -1
   const float* row = p.scores + static_cast<int64_t>(b) * p.score_stride;
   const unsigned int* ghist = p.hist + static_cast<int64_t>(b) * kBins;
   const int K = L < kTopK ? L : kTopK;
@@ -905,7 +909,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
       sort_desc_2048(sel, stage, hist, warp_tot, reinterpret_cast<uint32_t*>(stage + kTopK), &res[5]);
 
   int32_t* out = p.out + static_cast<int64_t>(b) * kTopK;
-  const int32_t* bt = p.block_table + static_cast<int64_t>(b) * p.max_pages;
+  const int32_t* bt = p.block_table + static_cast<int64_t>(bt_row < 0 ? 0 : bt_row) * p.max_pages;
   for (int i = tid; i < kTopK; i += kSelThreads) {
     int32_t v = -1;
     if (i < K) {
@@ -918,8 +922,41 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
 
 std::once_flag g_attr_once[64];
 int g_attr_status[64];
+std::once_flag g_sel_attr_once[64];
+int g_sel_attr_status[64];
 
 }  // namespace ix
+
+int launch_topk_select(const float* scores, const unsigned int* hist, const int32_t* seq_lens,
+                       const int32_t* block_table, const int32_t* row_req, int32_t* out, int rows,
+                       int score_stride, int max_pages, unsigned int* status, const DeviceInfo& info,
+                       cudaStream_t s) {
+  if (ix::kSelSmem > info.max_smem_optin) return DSA_ERR_UNSUPPORTED_DEVICE;
+  std::call_once(ix::g_sel_attr_once[info.device], [&]() {
+    ix::g_sel_attr_status[info.device] =
+        cudaFuncSetAttribute(ix::topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(ix::kSelSmem)) == cudaSuccess
+            ? DSA_OK
+            : DSA_ERR_CUDA;
+  });
+  if (ix::g_sel_attr_status[info.device] != DSA_OK) return ix::g_sel_attr_status[info.device];
+  ix::SelectParams selp;
+  selp.scores = scores;
+  selp.row_req = row_req;
+  selp.status = status;
+  selp.hist = hist;
+  selp.seq_lens = seq_lens;
+  selp.block_table = block_table;
+  selp.out = out;
+  selp.score_stride = score_stride;
+  selp.max_pages = max_pages;
+  if (launch_programmatic(ix::topk_select_kernel, dim3(rows), dim3(ix::kSelThreads), ix::kSelSmem, s,
+                          selp) != cudaSuccess)
+    return DSA_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  return DSA_OK;
+}
+
 }  // namespace dsa
 
 using namespace dsa;
@@ -960,9 +997,6 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
     bool ok = cudaFuncSetAttribute(ix::indexer_score_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(info.max_smem_optin)) == cudaSuccess;
-    ok = ok && cudaFuncSetAttribute(ix::topk_select_kernel,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(ix::kSelSmem)) == cudaSuccess;
     ix::g_attr_status[info.device] = ok ? DSA_OK : DSA_ERR_CUDA;
   });
   if (ix::g_attr_status[info.device] != DSA_OK) return ix::g_attr_status[info.device];
@@ -995,17 +1029,6 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
   sp.score_stride = max_pages * ix::kPage;
   ix::indexer_score_kernel<<<info.num_sms, ix::kThreads, smem1, s>>>(kmap, qmap, sp);
 
-  ix::SelectParams selp;
-  selp.scores = sp.scores;
-  selp.hist = sp.hist;
-  selp.seq_lens = seq_lens;
-  selp.block_table = block_table;
-  selp.out = topk_indices;
-  selp.score_stride = sp.score_stride;
-  selp.max_pages = max_pages;
-  if (launch_programmatic(ix::topk_select_kernel, dim3(batch), dim3(ix::kSelThreads), ix::kSelSmem,
-                          s, selp) != cudaSuccess)
-    return DSA_ERR_CUDA;
-  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
-  return DSA_OK;
+  return launch_topk_select(sp.scores, sp.hist, seq_lens, block_table, nullptr, topk_indices, batch,
+                            sp.score_stride, max_pages, sp.status, info, s);
 }

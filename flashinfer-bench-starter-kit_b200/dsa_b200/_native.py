@@ -36,6 +36,11 @@ SIGNATURES = {
                                                ctypes.c_int32, _P, _P]),
     "dsa_index_cache_write": (ctypes.c_int, [_P, _P, ctypes.c_int32, _P, ctypes.c_int64,
                                              ctypes.c_int32, _P, _P]),
+    "dsa_indexer_prefill_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32,
+                                                              ctypes.c_int32]),
+    "dsa_indexer_prefill_run": (ctypes.c_int, [_P, _P, ctypes.c_int64, _P, _P, _P, _P, ctypes.c_int32,
+                                               ctypes.c_int32, ctypes.c_int32, _P, _P, ctypes.c_size_t,
+                                               _P]),
 }
 
 _lib = None

@@ -103,12 +103,73 @@ def run(q_index_fp8: torch.Tensor, k_index_cache_fp8: torch.Tensor, weights: tor
         raise_on_device_status(dev)
 
 
+@torch.no_grad()
+def run_prefill(q_index_fp8: torch.Tensor, k_index_cache_fp8: torch.Tensor, weights: torch.Tensor,
+                seq_lens: torch.Tensor, block_table: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                topk_indices: torch.Tensor) -> None:
+    """Indexer for many query rows per request (prefill / chunked prefill).
+
+    Row t of request r (rows ``cu_seqlens_q[r] .. cu_seqlens_q[r+1]-1``) is
+    the decode problem ``run`` solves for ``(q[t], weights[t], seq_lens[t],
+    block_table[r])``; causal rows of a chunk pass growing ``seq_lens``.  The
+    rows of a request are scored four at a time as one FP8 GEMM, so each K
+    tile is read once per four rows instead of once per row.
+    """
+    dev = q_index_fp8.device
+    _require(dev.type == "cuda", "tensors must be on a CUDA device")
+    for name, t in (("k_index_cache_fp8", k_index_cache_fp8), ("weights", weights),
+                    ("seq_lens", seq_lens), ("block_table", block_table),
+                    ("cu_seqlens_q", cu_seqlens_q), ("topk_indices", topk_indices)):
+        _require(t.device == dev, f"{name} is on {t.device}, expected {dev}")
+    _require(q_index_fp8.dtype == torch.float8_e4m3fn,
+             f"q_index_fp8 must be float8_e4m3fn, got {q_index_fp8.dtype}")
+    _require(q_index_fp8.dim() == 3 and tuple(q_index_fp8.shape[1:]) == (NUM_HEADS, HEAD_DIM),
+             f"q_index_fp8 must be [T, {NUM_HEADS}, {HEAD_DIM}], got {tuple(q_index_fp8.shape)}")
+    T = q_index_fp8.shape[0]
+    _require(weights.dtype == torch.float32 and tuple(weights.shape) == (T, NUM_HEADS),
+             f"weights must be float32 [{T}, {NUM_HEADS}]")
+    _require(seq_lens.dtype == torch.int32 and tuple(seq_lens.shape) == (T,),
+             f"seq_lens must be int32 [{T}]")
+    _require(block_table.dim() == 2 and block_table.shape[1] >= 1, "block_table must be [R, max_pages]")
+    _require(block_table.dtype in (torch.int32, torch.int64), "block_table must be int32 or int64")
+    R = block_table.shape[0]
+    _require(cu_seqlens_q.dtype in (torch.int32, torch.int64) and tuple(cu_seqlens_q.shape) == (R + 1,),
+             f"cu_seqlens_q must be int32 [{R + 1}] (one more than block_table rows)")
+    _require(topk_indices.dtype == torch.int32 and tuple(topk_indices.shape) == (T, TOPK),
+             f"topk_indices must be int32 [{T}, {TOPK}]")
+    _require(topk_indices.is_contiguous(), "topk_indices must be contiguous (written in place)")
+    num_pages = num_pages_of(k_index_cache_fp8)
+    if T == 0:
+        return
+    _require(1 <= R <= T, f"need 1 <= requests <= rows, got {R} requests for {T} rows")
+    q = q_index_fp8.contiguous()
+    k = k_index_cache_fp8.contiguous()
+    w = weights.contiguous()
+    sl = seq_lens.contiguous()
+    bt = block_table.to(torch.int32).contiguous()
+    cu = cu_seqlens_q.to(torch.int32).contiguous()
+    max_pages = bt.shape[1]
+
+    L = _native.lib()
+    nbytes = L.dsa_indexer_prefill_workspace_bytes(T, R, max_pages)
+    cur = torch.cuda.current_stream(dev).cuda_stream
+    ws = workspace.get(dev, "indexer_prefill", nbytes, cur)
+    stream = ctypes.c_void_p(cur)
+    with torch.cuda.device(dev):
+        st = L.dsa_indexer_prefill_run(_ptr(q), _ptr(k), num_pages, _ptr(w), _ptr(sl), _ptr(bt),
+                                       _ptr(cu), T, R, max_pages, _ptr(topk_indices), _ptr(ws),
+                                       ws.numel(), stream)
+    _native.check(st, "dsa_indexer_prefill_run")
+    if _CHECK and not torch.cuda.is_current_stream_capturing():
+        raise_on_device_status(dev)
+
+
 def device_status(device: torch.device, clear: bool = True) -> int:
     """OR of the sticky device status bits of every indexer workspace on
     `device` (synchronises)."""
     bits = 0
     stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
-    for ws in workspace.buffers_of(device, "indexer"):
+    for ws in workspace.buffers_of(device, "indexer") + workspace.buffers_of(device, "indexer_prefill"):
         out = ctypes.c_uint32(0)
         with torch.cuda.device(device):
             st = _native.lib().dsa_read_device_status(_ptr(ws), ctypes.byref(out), int(clear),

@@ -190,6 +190,53 @@ def make_decode_inputs(seq_lens: list, seed: int = 0, device="cuda",
     return DecodeInputs(ix, qn, qp, ckv, kpe, 1.0 / math.sqrt(192.0))
 
 
+@dataclass
+class PrefillInputs:
+    """Query rows of several requests over paged FP8 K caches (prefill)."""
+    q_index_fp8: torch.Tensor        # [T, 64, 128] float8_e4m3fn
+    k_index_cache_fp8: torch.Tensor  # [pages, 64, 1, 132] uint8
+    weights: torch.Tensor            # [T, 64] float32
+    seq_lens: torch.Tensor           # [T] int32, causal lengths
+    block_table: torch.Tensor        # [R, max_pages] int32
+    cu_seqlens_q: torch.Tensor       # [R + 1] int32
+
+    @property
+    def num_pages(self) -> int:
+        return self.k_index_cache_fp8.shape[0]
+
+
+def make_prefill_inputs(prefixes: list, chunks: list, seed: int = 0, device="cuda",
+                        extra_pages: int = 0) -> PrefillInputs:
+    """Request r has `prefixes[r]` cached tokens and appends `chunks[r]` query
+    tokens; query t of the chunk sees positions <= prefix + t (causal), so its
+    row's length is prefix + t + 1.  Requests own disjoint pages of one pool."""
+    cpu, dev = _gens(seed, device)
+    totals = [p + c for p, c in zip(prefixes, chunks)]
+    need = pages_needed(totals)
+    pool = sum(need) + extra_pages
+    bt = page_tables(totals, pool, cpu, disjoint=True)
+    lens = [p + t + 1 for p, c in zip(prefixes, chunks) for t in range(c)]
+    T = len(lens)
+    cu = [0]
+    for c in chunks:
+        cu.append(cu[-1] + c)
+    q = torch.randn(T, IX_HEADS, IX_DIM, generator=dev, device=device, dtype=torch.float32)
+    q8, q_scale = quantize_q(q.to(torch.bfloat16))
+    del q
+    rows = torch.randn(pool * PAGE, IX_DIM, generator=dev, device=device,
+                       dtype=torch.float32).to(torch.bfloat16)
+    kc = quantize_pages(rows)
+    del rows
+    w = torch.randn(T, IX_HEADS, generator=dev, device=device, dtype=torch.float32) / 8.0 * q_scale
+    return PrefillInputs(q8, kc, w, torch.tensor(lens, dtype=torch.int32, device=device),
+                         bt.to(device), torch.tensor(cu, dtype=torch.int32, device=device))
+
+
+def prefill_flops(seq_lens: list) -> int:
+    """FP8 MACs x 2 of the per-row scores actually needed (each row's own length)."""
+    return sum(2 * IX_HEADS * IX_DIM * max(0, int(L)) for L in seq_lens)
+
+
 # ------------------------------------------------------------ byte model
 def indexer_bytes(seq_lens: list) -> int:
     """Algorithmic HBM bytes of one indexer call: 132 B per context token

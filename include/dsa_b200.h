@@ -173,6 +173,42 @@ DSA_API int dsa_indexer_run_noalloc(const void* q_index_fp8, const void* k_index
                                     int32_t batch, int32_t max_pages, int32_t* topk_indices,
                                     void* stream);
 
+/* Bytes of device workspace dsa_indexer_prefill_run needs: a 256-byte header,
+ * a [num_rows, 2048] uint32 radix histogram (cleared by the call), [num_rows,
+ * max_pages*64] fp32 score rows and the row-group plan (about
+ * (num_rows + 3*num_requests)/4 groups of 16 bytes, plus 4 bytes per row and
+ * per request).  Zero-fill it once before its first use. */
+DSA_API size_t dsa_indexer_prefill_workspace_bytes(int32_t num_rows, int32_t num_requests,
+                                                   int32_t max_pages);
+
+/* FP8 lightning indexer for many query rows per request (prefill, chunked
+ * prefill, speculative rows): row t of request r is the decode problem
+ * (q[t], weights[t], seq_lens[t], block_table[r]).
+ *
+ *   q_index_fp8       [num_rows, 64, 128] float8_e4m3fn, 16-byte aligned
+ *   k_index_cache_fp8 as for dsa_indexer_run
+ *   weights           [num_rows, 64] fp32, 16-byte aligned
+ *   seq_lens          [num_rows] int32: tokens row t sees (causal rows of a
+ *                     prefill chunk see growing prefixes)
+ *   block_table       [num_requests, max_pages] int32
+ *   cu_seqlens_q      [num_requests + 1] int32: request r owns rows
+ *                     [cu_seqlens_q[r], cu_seqlens_q[r+1]); 0 and num_rows
+ *                     at the ends (a violation sets DSA_DEV_BAD_SEQ_LEN)
+ *   topk_indices      [num_rows, 2048] int32 output, as for dsa_indexer_run
+ *
+ * Rows are scored four at a time per request as one FP8 tensor-core GEMM
+ * (N = 4 rows x 64 heads), so each 128-token K tile is read once per four
+ * rows.  With cu_seqlens_q = 0..num_rows it computes exactly what
+ * dsa_indexer_run computes.  No counterpart in the reference, whose indexer
+ * definition is decode-only (one query per request). */
+DSA_API int dsa_indexer_prefill_run(const void* q_index_fp8, const void* k_index_cache_fp8,
+                                    int64_t num_pages, const float* weights,
+                                    const int32_t* seq_lens, const int32_t* block_table,
+                                    const int32_t* cu_seqlens_q, int32_t num_rows,
+                                    int32_t num_requests, int32_t max_pages,
+                                    int32_t* topk_indices, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
 /* Quantises new indexer keys into the paged FP8 K cache (the step before
  * dsa_indexer_run in a serving loop).
  *

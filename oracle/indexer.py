@@ -151,3 +151,26 @@ def indexer_reference(q_index_fp8: torch.Tensor, k_index_cache_fp8: torch.Tensor
         phys = bt[b].numpy()[order // PAGE_SIZE]
         out[b, : order.shape[0]] = (phys * PAGE_SIZE + order % PAGE_SIZE).astype(np.int32)
     return torch.from_numpy(out), all_scores
+
+
+def rows_block_table(block_table: torch.Tensor, cu_seqlens_q: torch.Tensor, rows) -> torch.Tensor:
+    """Block-table row of each query row in `rows`: request r owns rows
+    cu_seqlens_q[r] .. cu_seqlens_q[r+1]-1."""
+    cu = cu_seqlens_q.cpu().to(torch.int64)
+    bt = block_table.cpu()
+    req = torch.searchsorted(cu, torch.as_tensor(list(rows), dtype=torch.int64), right=True) - 1
+    return bt[req]
+
+
+def prefill_reference(q_index_fp8: torch.Tensor, k_index_cache_fp8: torch.Tensor,
+                      weights: torch.Tensor, seq_lens: torch.Tensor, block_table: torch.Tensor,
+                      cu_seqlens_q: torch.Tensor, rows=None, topk: int = TOPK):
+    """Many query rows per request: row t of request r is the decode problem
+    (q[t], weights[t], seq_lens[t], block_table[r]), so this is
+    ``indexer_reference`` on the selected rows with each row's request's
+    block-table row.  The reference's indexer definition is decode-only
+    (one query per request, kernel.py:364); this is that computation applied
+    row by row.  Returns (topk_indices [len(rows), topk], scores list)."""
+    rows = list(range(q_index_fp8.shape[0])) if rows is None else list(rows)
+    return indexer_reference(q_index_fp8[rows], k_index_cache_fp8, weights[rows], seq_lens[rows],
+                             rows_block_table(block_table, cu_seqlens_q, rows), topk)
