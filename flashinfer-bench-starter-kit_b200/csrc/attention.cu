@@ -37,7 +37,8 @@
 //   own tiles are done, with all of its threads:
 //   lse = log2 L + M with L = sum_i l_i 2^(m_i - M),
 //   out = sum_i (O_i / l_i) l_i 2^(m_i - M) / L.
-//   The counters are cleared by an async memset at the start of every call.
+//   The counters sit at the end of the workspace; the merging CTA resets its
+//   token's counter, so they are zero between calls (no memset).
 #include <cuda_bf16.h>
 
 #include <cmath>

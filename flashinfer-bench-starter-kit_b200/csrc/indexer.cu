@@ -541,6 +541,9 @@ __device__ __forceinline__ int block_scan_incl(int v, int* warp_tot) {
 // need-th largest element; res = {d, count strictly above d, hist[d]}.
 __device__ __forceinline__ void find_bin(const uint32_t* hist, int need, int* warp_tot, int* res) {
   const int t = threadIdx.x;
+  // Defined even if the histogram holds fewer than `need` keys (it cannot
+  // when it matches the scores; the output stage checks every token).
+  if (t == 0) { res[0] = 0; res[1] = 0; res[2] = 0; }
   const int hi = kBins - 1 - 2 * t, lo = hi - 1;
   const int a = static_cast<int>(hist[hi]), c = static_cast<int>(hist[lo]);
   const int incl = block_scan_incl(a + c, warp_tot);
@@ -892,7 +895,10 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
       int pos = incl - cnt;
       for (int j = lane; j < avail; j += 32) {
         const uint64_t c = area[j];
-        if ((c & mask) >= prefix) sel[pos++] = c;
+        if ((c & mask) >= prefix) {
+          if (pos < kTopK) sel[pos] = c;
+          ++pos;
+        }
       }
     } else {
       const int Lr = (L + 31) & ~31;
@@ -914,7 +920,11 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     int32_t v = -1;
     if (i < K) {
       const int tok = static_cast<int>(~static_cast<uint32_t>(sorted[i]));
-      v = __ldg(bt + (tok >> 6)) * kPage + (tok & 63);
+      if (tok >= 0 && tok < L) {
+        v = __ldg(bt + (tok >> 6)) * kPage + (tok & 63);
+      } else {  // only if the histogram did not match the scores
+        atomicOr(p.status, DSA_DEV_STALE_WORKSPACE);
+      }
     }
     out[i] = v;
   }

@@ -16,18 +16,19 @@
 //       row), their prefix sums, and the request of every row.
 //   prefill_score_kernel (persistent, one CTA per SM)  the (group, tile)
 //       units are cut into equal contiguous slices.  Roles:
-//         warps 8,9   TMA producers (alternate tiles): two 64-token FP8 pages
+//         warps 16,17 TMA producers (alternate tiles): two 64-token FP8 pages
 //                     (128-byte swizzle) into a 6-stage ring, their fp32
 //                     scales into an 8-slot ring.
-//         warps 10,11 MMA issuers (alternate tiles): tcgen05.mma
+//         warps 18,19 MMA issuers (alternate tiles): tcgen05.mma
 //                     kind::f8f6f4, M = 128 tokens, N = 256 (4 rows x 64
 //                     heads), K = 128 (4 x K32), fp32 accumulators in TMEM
-//                     (2 stages x 256 columns = all 512).  Warp 10 also loads
+//                     (2 stages x 256 columns = all 512).  Warp 18 also loads
 //                     a group's q rows (one 32 KB TMA box) and weights.
-//         warps 0-7   epilogue: warp w reads TMEM sub-partition w & 3 (token
-//                     rows) for the two query rows 2*(w >> 2) + {0, 1}:
-//                     sum_h w_h * relu(scale * acc_h) per token in registers,
-//                     then the fp32 score and its radix-histogram count.
+//         warps 0-15  epilogue: warp w reads TMEM sub-partition w & 3 (token
+//                     rows) for query row w >> 2: sum_h w_h * relu(scale *
+//                     acc_h) per token in registers, then the fp32 score and
+//                     its radix-histogram count.  Four warps per scheduler
+//                     keep enough independent FMA chains in flight.
 //   topk_select_kernel (indexer.cu), one CTA per row, with the row's request
 //       resolving its block-table row.
 #include <mutex>
@@ -56,12 +57,12 @@ constexpr int kScaleSlots = kStages + kAccStages;         // 8 (see the decode k
 constexpr int kQBytes = kN * kDim;                        // 32768
 constexpr int kWBytes = kGroupRows * kHeads * 4;          // 1024
 constexpr int kBins = 2048;
-constexpr int kEpiWarps = 8;
-constexpr int kProdWarp0 = 8;
+constexpr int kEpiWarps = 16;                             // four per TMEM sub-partition
+constexpr int kProdWarp0 = 16;
 constexpr int kProdWarps = 2;
-constexpr int kMmaWarp0 = 10;
+constexpr int kMmaWarp0 = 18;
 constexpr int kMmaWarps = 2;
-constexpr int kThreads = 32 * (kMmaWarp0 + kMmaWarps);    // 384
+constexpr int kThreads = 32 * (kMmaWarp0 + kMmaWarps);    // 640
 constexpr int kPlanThreads = 1024;
 constexpr int kMaxRows = 1 << 20;
 
@@ -72,7 +73,7 @@ constexpr int kOffQ = kOffStage + kStages * kStageBytes;              // 98304
 constexpr int kOffW = kOffQ + 2 * kQBytes;                            // 163840
 constexpr int kOffScale = kOffW + 2 * kWBytes;                        // 165888
 constexpr int kOffHist = kOffScale + kScaleSlots * 2 * kScaleBytes;   // 169984
-constexpr int kOffBar = kOffHist + 2 * 2 * kBins * 4;                 // 202752
+constexpr int kOffBar = kOffHist + kGroupRows * kBins * 4;            // 202752
 constexpr int kOffMisc = kOffBar + 256;
 constexpr int kOffInfo = kOffMisc + 64;                               // producer warps x 32 tiles
 constexpr int kSmemBytes = 1024 + kOffInfo + kProdWarps * 32 * 12;
@@ -306,7 +307,7 @@ prefill_score_kernel(const __grid_constant__ CUtensorMap kmap,
   if (warp == kProdWarp0 && lane == 0) { prefetch_tensor_map(&kmap); prefetch_tensor_map(&qmap); }
   if (warp == kMmaWarp0) tmem_alloc(tmem_base_smem, kTmemCols);
   if (warp < kEpiWarps)
-    for (int i = tid; i < 2 * 2 * kBins; i += 32 * kEpiWarps) hist_all[i] = 0;
+    for (int i = tid; i < kGroupRows * kBins; i += 32 * kEpiWarps) hist_all[i] = 0;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -403,7 +404,7 @@ prefill_score_kernel(const __grid_constant__ CUtensorMap kmap,
     __syncwarp();
   } else if (warp >= kMmaWarp0) {
     // ------------------------------------------------------ MMA issuers
-    // Warp 10+r issues the tiles n with n % 2 == r (accumulator r); warp 10
+    // Warp 18+r issues the tiles n with n % 2 == r (accumulator r); warp 18
     // also loads each group's q rows and weights once both issuers and all
     // epilogue warps released the slot.
     const int r = warp - kMmaWarp0;
@@ -458,48 +459,39 @@ prefill_score_kernel(const __grid_constant__ CUtensorMap kmap,
   } else {
     // ------------------------------------------------------ epilogue warps
     const int sp = warp & 3;           // TMEM sub-partition: token rows 32*sp .. +31
-    const int set = warp >> 2;         // query rows 2*set, 2*set + 1 of the group
+    const int q = warp >> 2;           // query row of the group
     const int row = sp * 32 + lane;    // token row of the tile
-    uint32_t* hist = hist_all + set * 2 * kBins;
-    const uint32_t bar_id = 1 + set;   // named barrier of the set's four warps
+    uint32_t* hist = hist_all + q * kBins;
+    const uint32_t bar_id = 1 + q;     // named barrier of row q's four warps
     if (nt > 0) {
       Cursor cur;
       cur.start(p.tile_off, ngroups, u0);
       Group gr{};
-      int L[2] = {0, 0};
+      int L = 0;
       int nq = 0;
-      // Adds the set's counts into the global histograms of its two rows
-      // and clears them (all four warps of the set, after their last tile
-      // of the group).
+      // Adds row q's counts into its global histogram and clears them (all
+      // four warps of the row, after their last tile of the group).
       auto flush = [&]() {
         named_barrier_sync(bar_id, 128);
-        const int e = sp * 32 + lane;
-        for (int qq = 0; qq < 2; ++qq) {
-          const int q = 2 * set + qq;
-          if (q >= gr.nrows) continue;
+        if (q < gr.nrows) {
           unsigned int* g = p.hist + static_cast<int64_t>(gr.row0 + q) * kBins;
-          uint32_t* h = hist + qq * kBins;
-          for (int i = e; i < kBins; i += 128) {
-            const uint32_t c = h[i];
-            if (c) { atomicAdd(g + i, c); h[i] = 0; }
+          for (int i = sp * 32 + lane; i < kBins; i += 128) {
+            const uint32_t c = hist[i];
+            if (c) { atomicAdd(g + i, c); hist[i] = 0; }
           }
         }
         named_barrier_sync(bar_id, 128);
       };
       auto enter = [&]() {
         gr = p.groups[cur.g];
-#pragma unroll
-        for (int qq = 0; qq < 2; ++qq) {
-          const int q = 2 * set + qq;
-          L[qq] = q < gr.nrows ? clamp_len(__ldg(p.seq_lens + gr.row0 + q), max_len, p.status) : 0;
-        }
+        L = q < gr.nrows ? clamp_len(__ldg(p.seq_lens + gr.row0 + q), max_len, p.status) : 0;
       };
       enter();
       int slot = 0, sslot = 0;
       uint32_t aph = 0;
       bool ok = true;
       // After a wait gave up the loop keeps walking the tiles without
-      // waiting or working, so the four warps of a set still meet at the
+      // waiting or working, so the four warps of a row still meet at the
       // same flush barriers.
       for (int n = 0; n < nt; ++n) {
         if (n > 0 && cur.next(p.tile_off, ngroups)) {
@@ -523,56 +515,52 @@ prefill_score_kernel(const __grid_constant__ CUtensorMap kmap,
         tc_fence_after();
         const float scale =
             *reinterpret_cast<const float*>(smem + kOffScale + ss * 2 * kScaleBytes + row * 4);
-        const bool pos = scale > 0.f;
-        float sc[2] = {0.f, 0.f};
-        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + a * kN;
-#pragma unroll
-        for (int qq = 0; qq < 2; ++qq) {
-          const int q = 2 * set + qq;
-          if (q < gr.nrows) {  // uniform across the warp
-            const float* wq = w_mem + slot * (kWBytes / 4) + q * kHeads;
-            float f0 = 0.f, f1 = 0.f, g0 = 0.f;
-            float v[32];
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              tmem_ld32_wait(tbase + q * kHeads + 32 * half, v);
-              const float4* w4 = reinterpret_cast<const float4*>(wq + 32 * half);
-              if (pos) {
-#pragma unroll
-                for (int h4 = 0; h4 < 8; ++h4) {
-                  const float4 ww = w4[h4];
-                  f0 = fmaf(relu_nan(v[4 * h4 + 0]), ww.x, f0);
-                  f1 = fmaf(relu_nan(v[4 * h4 + 1]), ww.y, f1);
-                  f0 = fmaf(relu_nan(v[4 * h4 + 2]), ww.z, f0);
-                  f1 = fmaf(relu_nan(v[4 * h4 + 3]), ww.w, f1);
-                }
-              } else {
-#pragma unroll
-                for (int h4 = 0; h4 < 8; ++h4) {
-                  const float4 ww = w4[h4];
-                  const float wv[4] = {ww.x, ww.y, ww.z, ww.w};
-#pragma unroll
-                  for (int i = 0; i < 4; ++i) {
-                    const float x = v[4 * h4 + i] * scale;
-                    g0 += (x <= 0.f ? 0.f : x) * wv[i];
-                  }
-                }
-              }
-            }
-            sc[qq] = pos ? scale * (f0 + f1) : g0;
-          }
-        }
+        // Row q's 64 accumulator columns in one load; the accumulator is
+        // handed back before the math.
+        const uint32_t tbase =
+            tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + a * kN + q * kHeads;
+        float v[64];
+        tmem_ld32x2_wait(tbase, tbase + 32, v);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&accempty[a]);
-        const int tok = cur.j * kTileTok + row;
+        if (q >= gr.nrows) continue;  // uniform: the group has fewer rows
+        const float4* w4 = reinterpret_cast<const float4*>(w_mem + slot * (kWBytes / 4) + q * kHeads);
+        float sc;
+        if (scale > 0.f) {
+          // relu(scale * v) = scale * relu(v) for scale > 0.  The relu is
+          // taken doubled, v + |v| = 2 relu(v) (one add, NaN-propagating,
+          // -0 -> +0), and the doubled sum halved at the end: scaling by 2
+          // commutes with every fp32 rounding, so the score is bit-identical
+          // to sum_h w_h relu(v_h) with even and odd heads accumulated
+          // separately in head order, as in the decode kernel.
+          float f0 = 0.f, f1 = 0.f;
 #pragma unroll
-        for (int qq = 0; qq < 2; ++qq) {
-          if (tok < L[qq]) {
-            const int q = 2 * set + qq;
-            p.scores[static_cast<int64_t>(gr.row0 + q) * p.score_stride + tok] = sc[qq];
-            atomicAdd(&hist[qq * kBins + (score_key(sc[qq]) >> 21)], 1u);
+          for (int h4 = 0; h4 < 16; ++h4) {
+            const float4 ww = w4[h4];
+            fma2(f0, f1, relu2(v[4 * h4 + 0]), relu2(v[4 * h4 + 1]), ww.x, ww.y);
+            fma2(f0, f1, relu2(v[4 * h4 + 2]), relu2(v[4 * h4 + 3]), ww.z, ww.w);
           }
+          sc = scale * (0.5f * (f0 + f1));
+        } else {
+          // zero, negative or NaN scale: relu(scale * v) term by term
+          float g0 = 0.f;
+#pragma unroll
+          for (int h4 = 0; h4 < 16; ++h4) {
+            const float4 ww = w4[h4];
+            const float wv[4] = {ww.x, ww.y, ww.z, ww.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float x = v[4 * h4 + i] * scale;
+              g0 += (x <= 0.f ? 0.f : x) * wv[i];
+            }
+          }
+          sc = g0;
+        }
+        const int tok = cur.j * kTileTok + row;
+        if (tok < L) {
+          p.scores[static_cast<int64_t>(gr.row0 + q) * p.score_stride + tok] = sc;
+          atomicAdd(&hist[score_key(sc) >> 21], 1u);
         }
       }
       flush();

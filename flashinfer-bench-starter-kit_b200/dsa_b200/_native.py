@@ -86,5 +86,6 @@ def describe_device_status(bits: int) -> str:
     if bits & DEV_WAIT_TIMEOUT:
         names.append("a kernel pipeline wait timed out")
     if bits & DEV_STALE_WORKSPACE:
-        names.append("a workspace merge counter was not zero on entry (zero-fill the workspace)")
+        names.append("workspace contents inconsistent: a merge counter not zero on entry or a "
+                     "histogram not matching its scores (zero-fill the workspace)")
     return ", ".join(names) if names else "ok"

@@ -61,8 +61,9 @@ extern "C" {
 #define DSA_DEV_BAD_PAGE      0x2u  /* block_table entry outside [0, num_pages) */
 #define DSA_DEV_BAD_INDEX     0x4u  /* sparse index outside [-1, num_slots)     */
 #define DSA_DEV_WAIT_TIMEOUT  0x8u  /* a bounded pipeline wait gave up          */
-#define DSA_DEV_STALE_WORKSPACE 0x10u /* a merge counter was not zero on entry:   */
-                                      /* zero-fill the workspace again            */
+#define DSA_DEV_STALE_WORKSPACE 0x10u /* workspace contents did not match: a merge */
+                                      /* counter not zero on entry, or an indexer */
+                                      /* histogram not matching its scores        */
 
 /* Shape constants of the two contest definitions
  * dsa_topk_indexer_fp8_h64_d128_topk2048_ps64 and
