@@ -494,23 +494,24 @@ prefill_score_kernel(const __grid_constant__ CUtensorMap kmap,
       // waiting or working, so the four warps of a row still meet at the
       // same flush barriers.
       for (int n = 0; n < nt; ++n) {
+        bool new_group = n == 0;
         if (n > 0 && cur.next(p.tile_off, ngroups)) {
           flush();
           if (lane == 0) mbar_arrive(&qempty[(nq - 1) & 1]);
           enter();
+          new_group = true;
+        }
+        if (new_group) {  // the group's weights (with its q rows) must have landed
           slot = nq & 1;
           ++nq;
-        } else if (n == 0) {
-          slot = 0;
-          nq = 1;
+          ok = ok && __all_sync(0xffffffffu, mbar_wait(&qfull[slot], ((nq - 1) >> 1) & 1, wctx));
         }
         const int a = n & 1;
         const uint32_t par = aph;
         if (a == 1) aph ^= 1;
+        const int ss = sslot;  // this tile's scale slot
         if (++sslot == kScaleSlots) sslot = 0;
-        const int ss = sslot == 0 ? kScaleSlots - 1 : sslot - 1;  // this tile's scale slot
-        ok = ok && __all_sync(0xffffffffu, mbar_wait(&qfull[slot], ((nq - 1) >> 1) & 1, wctx) &&
-                                               mbar_wait(&accfull[a], par, wctx));
+        ok = ok && __all_sync(0xffffffffu, mbar_wait(&accfull[a], par, wctx));
         if (!ok) continue;
         tc_fence_after();
         const float scale =
