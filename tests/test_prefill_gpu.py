@@ -63,6 +63,24 @@ def test_prefill_small_matches_oracle(cuda_device, prefixes, chunks):
     assert rep.order_violations == 0
 
 
+def test_prefill_empty_requests_and_zero_length_rows(cuda_device):
+    # Requests with no rows (equal consecutive cu_seqlens_q entries), rows of
+    # length 0 inside a group, and a request whose rows span three groups.
+    pf = workloads.make_prefill_inputs([300, 2600, 0], [3, 9, 2], seed=31, device=cuda_device,
+                                       extra_pages=2)
+    R = pf.block_table.shape[0]
+    bt = torch.cat([pf.block_table[:1], pf.block_table[:1], pf.block_table[1:], pf.block_table[2:]])
+    cu = torch.tensor([0, 3, 3, 12, 12, 14], dtype=torch.int32, device=cuda_device)  # requests 1, 4 empty
+    assert bt.shape[0] == R + 2
+    pf.block_table, pf.cu_seqlens_q = bt.contiguous(), cu
+    pf.seq_lens[1] = 0      # a zero-length row in the first group
+    pf.seq_lens[7] = 0      # and one in the middle of the long request
+    got = run_prefill(pf)
+    T = pf.q_index_fp8.shape[0]
+    oracle_check(pf, got, list(range(T)))
+    assert (got[1] == -1).all() and (got[7] == -1).all()
+
+
 def test_prefill_equals_decode_kernel(cuda_device):
     # 3 requests, 4k-16k contexts, 37 rows: the GEMM-shaped path and the
     # decode path score with the same per-token arithmetic.
