@@ -734,6 +734,16 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
   const float* row = p.scores + static_cast<int64_t>(b) * p.score_stride;
   const unsigned int* ghist = p.hist + static_cast<int64_t>(b) * kBins;
   const int K = L < kTopK ? L : kTopK;
+  const float4* row4 = reinterpret_cast<const float4*>(row);
+  const int L4 = (L + 3) >> 2;  // float4s covering [0, L)
+  // The main pass's first scores need no threshold: their loads are in
+  // flight while the histogram is read and the boundary bin is found.
+  float4 nv[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int q = u * kSelThreads + tid;
+    nv[u] = (L > kTopK && q < L4) ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 
   // The histogram the score kernel accumulated for this request.
   for (int i = tid; i < kBins; i += kSelThreads) hist[i] = ghist[i];
@@ -761,21 +771,13 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     // Bins above +inf hold only NaN (every NaN has the top key): stage NaN
     // and +inf then; the refinement below drops the +inf keys again.
     if (thr != thr) thr = INFINITY;
-    const float4* row4 = reinterpret_cast<const float4*>(row);
-    const int L4 = (L + 3) >> 2;                         // float4s covering [0, L)
     uint64_t* mine = stage + warp * kStageCap;
     int wcount = 0;
     // find_bin has read the first-level histogram; it is rebuilt below as
     // the second-level one (next 11 bits of the boundary bin).
     for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
     // Loads run one round ahead of the compares, so the L2 latency of round
-    // r + 1 overlaps the work on round r.
-    float4 nv[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int q = u * kSelThreads + tid;
-      nv[u] = q < L4 ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    // r + 1 overlaps the work on round r (round 0's were issued on entry).
     for (int q0 = 0; q0 < L4; q0 += 4 * kSelThreads) {
       float4 v[4];
 #pragma unroll
