@@ -34,12 +34,14 @@
 //    encodes "score descending, then lower token index first" as one total
 //    order.  The score kernel's epilogue already histograms the top 11 key
 //    bits per request (per-warp shared-memory histograms flushed into a
-//    global [batch, 2048] table, cleared by an async memset at each call);
+//    global [batch, 2048] table, cleared at each call by a small kernel that
+//    the score kernel overlaps through programmatic launch);
 //    one pass over the L scores then moves the winners of higher bins to the
 //    output and the boundary bin to a shared-memory candidate list, which
 //    later passes refine.  The 2048
 //    winners are bitonic-sorted and translated to global slot ids through
 //    the block table (kernel.py:156-169), then -1 padded (kernel.py:206).
+#include <algorithm>
 #include <mutex>
 
 #include "host.h"
@@ -109,7 +111,7 @@ struct ScoreParams {
   const int32_t* seq_lens;
   const int32_t* block_table;
   float* scores;          // [batch][score_stride]
-  unsigned int* hist;     // [batch][kBins], cleared by an async memset at every call
+  unsigned int* hist;     // [batch][kBins], cleared by hist_clear_kernel at every call
   unsigned int* status;
   int64_t num_pages;
   int batch;
@@ -171,6 +173,16 @@ __device__ __forceinline__ TileInfo tile_info(const ScoreParams& p, const int* t
     t.p1 = t.npg == 2 ? page_id(p, t.b, 2 * t.j + 1) : 0;
   }
   return t;
+}
+
+// Zeroes n 16-byte words of the histogram rows.  The score kernel is
+// launched programmatically after it and only its epilogue warps wait for it
+// (griddep_wait), so the clearing overlaps the score kernel's start; the
+// lines it writes are in L2 when the epilogue's atomics reach them.
+__global__ void __launch_bounds__(256) hist_clear_kernel(uint4* p, int64_t n) {
+  griddep_launch_dependents();
+  for (int64_t i = blockIdx.x * 256 + threadIdx.x; i < n; i += static_cast<int64_t>(gridDim.x) * 256)
+    p[i] = make_uint4(0u, 0u, 0u, 0u);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -386,6 +398,9 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
     const int sp = warp & 3;          // TMEM sub-partition this warp may access
     const int row = sp * 32 + lane;   // token row of the 128-token tile
     uint32_t* hist = hist_all + warp * (kBins / 2);
+    // The score kernel is launched programmatically after the kernel that
+    // clears the global histograms; only these warps touch them.
+    griddep_wait();
     if (set < nt) {
       int b = 0, j = 0;
       locate(tile_off, p.batch, u0 + set, b, j);
@@ -1022,9 +1037,15 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
   if (st != DSA_OK) return st;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(static_cast<uint8_t*>(workspace) + kWorkspaceHeader, 0,
-                      sizeof(uint32_t) * static_cast<size_t>(batch) * ix::kBins, s) != cudaSuccess)
-    return DSA_ERR_CUDA;
+  {
+    // Launched normally: it starts after every earlier write to the inputs,
+    // so the score kernel (launched programmatically after it) may read them
+    // at once; only its histogram flushes wait for the clearing.
+    const int64_t n16 = static_cast<int64_t>(batch) * ix::kBins * 4 / 16;
+    const int blocks = static_cast<int>(std::min<int64_t>((n16 + 255) / 256, info.num_sms));
+    ix::hist_clear_kernel<<<blocks, 256, 0, s>>>(
+        reinterpret_cast<uint4*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeader), n16);
+  }
   ix::ScoreParams sp;
   sp.k_cache = static_cast<const uint8_t*>(k_index_cache_fp8);
   sp.weights = weights;
@@ -1039,7 +1060,9 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
   sp.batch = batch;
   sp.max_pages = max_pages;
   sp.score_stride = max_pages * ix::kPage;
-  ix::indexer_score_kernel<<<info.num_sms, ix::kThreads, smem1, s>>>(kmap, qmap, sp);
+  if (launch_programmatic(ix::indexer_score_kernel, dim3(info.num_sms), dim3(ix::kThreads), smem1, s,
+                          kmap, qmap, sp) != cudaSuccess)
+    return DSA_ERR_CUDA;
 
   return launch_topk_select(sp.scores, sp.hist, seq_lens, block_table, nullptr, topk_indices, batch,
                             sp.score_stride, max_pages, sp.status, info, s);

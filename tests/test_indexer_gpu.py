@@ -208,9 +208,17 @@ def test_long_context_config2(cuda_device):
 
 def test_workspace_reuse_across_sizes(cuda_device):
     # One stream, one workspace; growing the batch at a fixed workspace size
-    # moves the histogram region onto bytes that held scores before.
-    # Largest first, so later calls reuse (never regrow) the workspace.
+    # moves the histogram region onto bytes that held scores before (the 6-row
+    # call after the 2-row one): every call clears its histogram rows before
+    # the score kernel adds to them.  Largest first, so later calls reuse
+    # (never regrow) the workspace.
     for lens, mp in (([5000] * 9, 80), ([9000] * 2, 160), ([6000] * 6, 100), ([2100] * 4, 160)):
         ix = workloads.make_indexer_inputs(lens, pool_pages=512, seed=len(lens), device=cuda_device,
                                            max_pages=mp)
         oracle_check(ix, run_gpu(ix))
+    # Histograms left over from a previous call never leak into the next one:
+    # the same call twice gives the same result.
+    ix = workloads.make_indexer_inputs([6000] * 6, pool_pages=512, seed=6, device=cuda_device,
+                                       max_pages=100)
+    first = run_gpu(ix)
+    assert torch.equal(first, run_gpu(ix))
