@@ -363,7 +363,7 @@ def main() -> int:
                       "step_frac_of_peak": value / world / peak},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": 3 * K,  # score, select, attention kernels per step
+        "gpu_launches": 4 * K,  # histogram clear, score, select, attention kernels per step
         "clocks": clk.summary(),
         "verified": verified,
     }

@@ -85,9 +85,9 @@ DSA_API const char* dsa_b200_status_string(int status);
 
 /* Bytes of device workspace dsa_indexer_run needs for this batch and block
  * table width: a 256-byte header, a [batch, 2048] uint32 radix histogram
- * (cleared by the call itself with an async memset) and [batch,
- * max_pages*64] fp32 score rows.  Zero-fill a workspace once before its first
- * use so the status word in its header starts clear. */
+ * (cleared by the call itself, on its stream, before the scores are added)
+ * and [batch, max_pages*64] fp32 score rows.  Zero-fill a workspace once
+ * before its first use so the status word in its header starts clear. */
 DSA_API size_t dsa_indexer_workspace_bytes(int32_t batch, int32_t max_pages);
 
 /* FP8 lightning indexer, decode (one query token per request).
