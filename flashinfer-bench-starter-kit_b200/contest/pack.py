@@ -1,16 +1,26 @@
-"""Packs the B200 DSA kernels as contest CUDA solutions.
+"""Packs the B200 DSA kernels as contest solutions.
 
-    python flashinfer-bench-starter-kit_b200/contest/pack.py [-o OUT_DIR]
+    python flashinfer-bench-starter-kit_b200/contest/pack.py [-o OUT_DIR] [--variant V]
 
 For each operator directory (dsa_indexer/, dsa_attention/) the config.toml
 names the definition and the entry point; this writes
 OUT_DIR/<operator>/packed_solution.json in the Solution shape the starter
-kit's README documents (name, definition, author, spec with language
-"cuda", target hardware, entry point, dependencies, destination-passing
-style and binding, then the sources as path/content pairs), which the
+kit's README documents (name, definition, author, spec with language,
+target hardware, entry point, dependencies, destination-passing style and
+binding, then the sources as path/content pairs), which the
 evaluation pipeline uses directly when it finds it (FAQ.md:53-55).  The
 sources are the library's own files, flattened into one directory: the
-torch-binding entry points (contest/kernel.cu), the C ABI and the kernels.
+entry points, the C ABI and the kernels.  Three variants:
+
+  cuda     (default, the operators' config.toml) language "cuda", binding
+           "torch": contest/kernel.cu::dsa_indexer / ::dsa_attention.
+  tvm-ffi  language "cuda", binding "tvm-ffi" (the harness's default
+           binding): contest/kernel_tvm.cu::dsa_indexer / ::dsa_attention.
+  python   language "python": contest/kernel.py::run_indexer /
+           ::run_attention, which compile the packed CUDA sources for sm_100a
+           themselves through tvm_ffi.cpp.load.  The harness's CUDA builders
+           set no SM target and take no flags (FAQ.md:144-154), so this is the
+           variant that builds the sm_100a kernels under a stock harness.
 """
 
 from __future__ import annotations
@@ -23,8 +33,7 @@ import tomllib
 HERE = pathlib.Path(__file__).resolve().parent
 PKG = HERE.parent
 REPO = PKG.parent
-SOURCES = [
-    HERE / "kernel.cu",
+LIBRARY = [
     PKG / "csrc" / "capi.cu",
     PKG / "csrc" / "indexer.cu",
     PKG / "csrc" / "attention.cu",
@@ -33,34 +42,46 @@ SOURCES = [
     REPO / "include" / "dsa_b200.h",
 ]
 OPERATORS = ("dsa_indexer", "dsa_attention")
+# variant -> (language, binding, entry file, sources in front of the library,
+#             entry function per operator; None: the config.toml's)
+VARIANTS = {
+    "cuda": ("cuda", "torch", "kernel.cu", [HERE / "kernel.cu"], None),
+    "tvm-ffi": ("cuda", "tvm-ffi", "kernel_tvm.cu", [HERE / "kernel_tvm.cu"], None),
+    "python": ("python", None, "kernel.py", [HERE / "kernel.py", HERE / "kernel_tvm.cu"],
+               {"dsa_indexer": "run_indexer", "dsa_attention": "run_attention"}),
+}
 
 
-def solution(op: str) -> dict:
+def solution(op: str, variant: str = "cuda") -> dict:
     cfg = tomllib.loads((HERE / op / "config.toml").read_text())
     sol, build = cfg["solution"], cfg["build"]
+    language, binding, entry_file, front, fns = VARIANTS[variant]
+    fn = fns[op] if fns else build["entry_point"].split("::")[1]
+    spec = {
+        "language": language,
+        "target_hardware": ["cuda"],
+        "entry_point": f"{entry_file}::{fn}",
+        "dependencies": [],
+        "destination_passing_style": bool(build.get("destination_passing_style", True)),
+    }
+    if binding is not None:
+        spec["binding"] = binding
     return {
-        "name": sol["name"],
+        "name": sol["name"] if variant == "cuda" else f"{sol['name']}-{variant}",
         "definition": sol["definition"],
         "author": sol["author"],
-        "spec": {
-            "language": build["language"],
-            "target_hardware": ["cuda"],
-            "entry_point": build["entry_point"],
-            "dependencies": [],
-            "destination_passing_style": bool(build.get("destination_passing_style", True)),
-            "binding": build.get("binding", "tvm-ffi"),
-        },
-        "sources": [{"path": p.name, "content": p.read_text()} for p in SOURCES],
+        "spec": spec,
+        "sources": [{"path": p.name, "content": p.read_text()} for p in front + LIBRARY],
     }
 
 
-def pack(out_dir: pathlib.Path) -> list:
+def pack(out_dir: pathlib.Path, variant: str = "cuda") -> list:
     written = []
     for op in OPERATORS:
         d = out_dir / op
         d.mkdir(parents=True, exist_ok=True)
         path = d / "packed_solution.json"
-        path.write_text(json.dumps(solution(op), indent=2))
+        path.write_text(json.dumps(solution(op, variant), indent=2))
         written.append(path)
     return written
 
@@ -68,8 +89,9 @@ def pack(out_dir: pathlib.Path) -> list:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("-o", "--out", type=pathlib.Path, default=HERE / "packed")
+    ap.add_argument("--variant", choices=sorted(VARIANTS), default="cuda")
     args = ap.parse_args()
-    for p in pack(args.out):
+    for p in pack(args.out, args.variant):
         print(p)
 
 
