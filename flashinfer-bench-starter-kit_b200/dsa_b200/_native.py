@@ -10,6 +10,8 @@ import ctypes
 import pathlib
 import threading
 
+import torch
+
 LIB_PATH = pathlib.Path(__file__).resolve().with_name("libdsa_b200.so")
 
 DSA_OK = 0
@@ -67,6 +69,21 @@ def lib() -> ctypes.CDLL:
                     fn.argtypes = args
                 _lib = handle
     return _lib
+
+
+def current_stream(device: torch.device) -> int:
+    """Raw handle of torch's current stream on a CUDA `device` (no Stream
+    object is built: this sits on every call's host path)."""
+    return torch._C._cuda_getCurrentRawStream(device.index)
+
+
+def call_on(device: torch.device, fn, *args):
+    """fn(*args) with `device` current; the device is switched (and restored)
+    only when another one is current."""
+    if torch._C._cuda_getDevice() == device.index:
+        return fn(*args)
+    with torch.cuda.device(device):
+        return fn(*args)
 
 
 def check(status: int, what: str) -> None:

@@ -47,57 +47,64 @@ def _require(cond: bool, msg: str) -> None:
 
 def num_pages_of(k_index_cache_fp8: torch.Tensor) -> int:
     nbytes = k_index_cache_fp8.numel() * k_index_cache_fp8.element_size()
-    _require(k_index_cache_fp8.element_size() == 1,
-             f"k_index_cache_fp8 must have a 1-byte dtype, got {k_index_cache_fp8.dtype}")
-    _require(nbytes % PAGE_BYTES == 0 and nbytes > 0,
-             f"k_index_cache_fp8 holds {nbytes} bytes, not a positive multiple of {PAGE_BYTES}")
+    if k_index_cache_fp8.element_size() != 1:
+        _fail(f"k_index_cache_fp8 must have a 1-byte dtype, got {k_index_cache_fp8.dtype}")
+    if nbytes % PAGE_BYTES != 0 or nbytes <= 0:
+        _fail(f"k_index_cache_fp8 holds {nbytes} bytes, not a positive multiple of {PAGE_BYTES}")
     return nbytes // PAGE_BYTES
+
+
+def _fail(msg: str) -> None:
+    raise ValueError(f"dsa_indexer.run: {msg}")
 
 
 @torch.no_grad()
 def run(q_index_fp8: torch.Tensor, k_index_cache_fp8: torch.Tensor, weights: torch.Tensor,
         seq_lens: torch.Tensor, block_table: torch.Tensor, topk_indices: torch.Tensor) -> None:
+    # Every message is formatted only on failure: this runs once per decode step.
     dev = q_index_fp8.device
-    _require(dev.type == "cuda", "tensors must be on a CUDA device")
+    if dev.type != "cuda":
+        _fail("tensors must be on a CUDA device")
     for name, t in (("k_index_cache_fp8", k_index_cache_fp8), ("weights", weights),
                     ("seq_lens", seq_lens), ("block_table", block_table),
                     ("topk_indices", topk_indices)):
-        _require(t.device == dev, f"{name} is on {t.device}, expected {dev}")
-    _require(q_index_fp8.dtype == torch.float8_e4m3fn,
-             f"q_index_fp8 must be float8_e4m3fn, got {q_index_fp8.dtype}")
-    _require(q_index_fp8.dim() == 3 and tuple(q_index_fp8.shape[1:]) == (NUM_HEADS, HEAD_DIM),
-             f"q_index_fp8 must be [B, {NUM_HEADS}, {HEAD_DIM}], got {tuple(q_index_fp8.shape)}")
+        if t.device != dev:
+            _fail(f"{name} is on {t.device}, expected {dev}")
+    if q_index_fp8.dtype != torch.float8_e4m3fn:
+        _fail(f"q_index_fp8 must be float8_e4m3fn, got {q_index_fp8.dtype}")
+    if q_index_fp8.dim() != 3 or q_index_fp8.shape[1:] != (NUM_HEADS, HEAD_DIM):
+        _fail(f"q_index_fp8 must be [B, {NUM_HEADS}, {HEAD_DIM}], got {tuple(q_index_fp8.shape)}")
     B = q_index_fp8.shape[0]
-    _require(weights.dtype == torch.float32 and tuple(weights.shape) == (B, NUM_HEADS),
-             f"weights must be float32 [{B}, {NUM_HEADS}]")
-    _require(seq_lens.dtype == torch.int32 and tuple(seq_lens.shape) == (B,),
-             f"seq_lens must be int32 [{B}]")
-    _require(block_table.dim() == 2 and block_table.shape[0] == B and block_table.shape[1] >= 1,
-             f"block_table must be [{B}, max_pages]")
-    _require(block_table.dtype in (torch.int32, torch.int64), "block_table must be int32 or int64")
-    _require(topk_indices.dtype == torch.int32 and tuple(topk_indices.shape) == (B, TOPK),
-             f"topk_indices must be int32 [{B}, {TOPK}]")
-    _require(topk_indices.is_contiguous(), "topk_indices must be contiguous (written in place)")
+    if weights.dtype != torch.float32 or weights.shape != (B, NUM_HEADS):
+        _fail(f"weights must be float32 [{B}, {NUM_HEADS}]")
+    if seq_lens.dtype != torch.int32 or seq_lens.shape != (B,):
+        _fail(f"seq_lens must be int32 [{B}]")
+    if block_table.dim() != 2 or block_table.shape[0] != B or block_table.shape[1] < 1:
+        _fail(f"block_table must be [{B}, max_pages]")
+    if block_table.dtype != torch.int32 and block_table.dtype != torch.int64:
+        _fail("block_table must be int32 or int64")
+    if topk_indices.dtype != torch.int32 or topk_indices.shape != (B, TOPK):
+        _fail(f"topk_indices must be int32 [{B}, {TOPK}]")
+    if not topk_indices.is_contiguous():
+        _fail("topk_indices must be contiguous (written in place)")
     num_pages = num_pages_of(k_index_cache_fp8)
     if B == 0:
         return
-    # The reference calls .contiguous() on every input (kernel.py:365-368)
-    # and converts the block table to int32 (kernel.py:210).
     q = q_index_fp8.contiguous()
     k = k_index_cache_fp8.contiguous()
     w = weights.contiguous()
     sl = seq_lens.contiguous()
-    bt = block_table.to(torch.int32).contiguous()
+    bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+    bt = bt.contiguous()
     max_pages = bt.shape[1]
 
     L = _native.lib()
     nbytes = L.dsa_indexer_workspace_bytes(B, max_pages)
-    cur = torch.cuda.current_stream(dev).cuda_stream
+    cur = _native.current_stream(dev)
     ws = workspace.get(dev, "indexer", nbytes, cur)
-    stream = ctypes.c_void_p(cur)
-    with torch.cuda.device(dev):
-        st = L.dsa_indexer_run(_ptr(q), _ptr(k), num_pages, _ptr(w), _ptr(sl), _ptr(bt), B,
-                               max_pages, _ptr(topk_indices), _ptr(ws), ws.numel(), stream)
+    st = _native.call_on(dev, L.dsa_indexer_run, q.data_ptr(), k.data_ptr(), num_pages, w.data_ptr(),
+                         sl.data_ptr(), bt.data_ptr(), B, max_pages, topk_indices.data_ptr(),
+                         ws.data_ptr(), ws.numel(), cur)
     _native.check(st, "dsa_indexer_run")
     if _CHECK and not torch.cuda.is_current_stream_capturing():
         raise_on_device_status(dev)
