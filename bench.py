@@ -16,6 +16,9 @@ Workloads (seeded synthetic data with the contest shapes):
   config3     a prefill chunk: one request, 4096 query rows appended to a
               61440-token prefix (causal), indexer rows scored as one FP8
               GEMM, then attention for all 4096 rows; one replica per GPU.
+  cache_write the indexer K cache populated: 64 requests x 65536 tokens per GPU
+              (--batch / --seq-len override) quantised into the paged FP8
+              cache by dsa_index_cache_write, one launch per step.
 
 Printed (rank 0, one JSON line): whole-job algorithmic HBM GB/s (value), the
 step time, the roofline of the dominant operator, the CPU oracle baseline,
@@ -51,7 +54,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["north_star", "config4", "config3"], default="north_star")
+    ap.add_argument("--workload", choices=["north_star", "config4", "config3", "cache_write"],
+                    default="north_star")
     ap.add_argument("--streams", type=int, default=1, help="streams inside the captured step")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
@@ -258,6 +262,8 @@ def main() -> int:
         raise SystemExit("--warmup must be >= 3")
     if args.workload == "config3":
         return run_config3(args, rank, world, local_rank)
+    if args.workload == "cache_write":
+        return run_cache_write(args, rank, world, local_rank)
 
     import torch.distributed as dist
 
@@ -645,6 +651,172 @@ def run_config3(args, rank: int, world: int, local_rank: int) -> int:
         "clocks": clk.summary(),
         "verified": bool(ok.item()),
         "parity_rows": {"rows": rows, "exact": rep.exact_rows, "swaps": rep.swaps},
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_cache_write(args, rank: int, world: int, local_rank: int) -> int:
+    """Indexer K-cache population: B requests x L tokens per GPU (default 64 x
+    65536, the cache the north-star indexer reads) quantised into the paged
+    FP8 cache, one dsa_index_cache_write launch per step, captured as a CUDA
+    graph.  Algorithmic bytes per token: 256 B of bf16 key + 8 B of slot read,
+    128 B of FP8 row + 4 B of scale written.  Each GPU writes its own cache
+    (weak scaling, no collective)."""
+    import torch.distributed as dist
+
+    from dsa_b200 import cache as kc
+    from dsa_b200 import sharding
+    from oracle import cache_write as ocw
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    B = args.batch or 64
+    L = args.seq_len // 64 * 64
+    n, ppr = B * L, L // 64
+    pool = B * ppr
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    k = torch.randn(n, 128, generator=g, device=dev).to(torch.bfloat16)
+    perm = torch.randperm(pool, generator=g, device=dev)   # request b's page j = perm[b*ppr + j]
+    tok = torch.arange(n, device=dev)
+    slots = perm[tok // 64] * 64 + tok % 64
+    del tok
+    cache = torch.zeros(pool * ocw.PAGE_BYTES, dtype=torch.uint8, device=dev)
+    per_tok = 256 + 8 + 128 + 4
+    rank_bytes = n * per_tok
+
+    def write():
+        kc.write_index_k(k, slots, cache)
+
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(cap):
+        write()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cap), torch.cuda.graph(gr, stream=cap):
+        write()
+    torch.cuda.current_stream(dev).wait_stream(cap)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        gr.replay()
+    torch.cuda.synchronize()
+    barrier()
+    K = args.steps
+    with ClockSampler(dev) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms_kernel = e0.elapsed_time(e1) / K
+
+    # End to end through write_index_k: every step copies its keys and slots
+    # from pinned host memory and reads the last written page back.
+    e2e = None
+    if not args.no_e2e:
+        hk = torch.empty(k.shape, dtype=k.dtype, pin_memory=True)
+        hk.copy_(k)
+        hs = torch.empty(slots.shape, dtype=slots.dtype, pin_memory=True)
+        hs.copy_(slots)
+        hpage = torch.empty(ocw.PAGE_BYTES, dtype=torch.uint8, pin_memory=True)
+        dk, ds = torch.empty_like(k), torch.empty_like(slots)
+        last = int(slots[-1]) // 64 * ocw.PAGE_BYTES
+
+        def one():
+            dk.copy_(hk, non_blocking=True)
+            ds.copy_(hs, non_blocking=True)
+            kc.write_index_k(dk, ds, cache)
+            hpage.copy_(cache[last:last + ocw.PAGE_BYTES], non_blocking=True)
+
+        for _ in range(3):
+            one()
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ke = max(1, min(K, 5))
+        a.record()
+        for _ in range(ke):
+            one()
+        b.record()
+        torch.cuda.synchronize()
+        ms_e = torch.tensor([a.elapsed_time(b) / ke], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ms_e, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * rank_bytes / (float(ms_e) * 1e-3) / 1e9, "unit": "GB/s",
+               "ms_per_step": float(ms_e), "h2d_bytes_per_step": hk.numel() * 2 + hs.numel() * 8,
+               "d2h_bytes_per_step": ocw.PAGE_BYTES, "steps": ke,
+               "api": "dsa_b200.cache.write_index_k (eager, ctypes -> C ABI) with the step's keys "
+                      "and slots copied from pinned host memory and one page read back"}
+
+    # Verification (outside the timed regions): the first and last request's
+    # first 64 pages against the oracle, byte for byte.
+    ok = True
+    view = cache.view(pool, ocw.PAGE_BYTES)
+    for b in (0, B - 1):
+        t0 = b * L
+        m = min(L, 4096)
+        want = ocw.write_cache(k[t0:t0 + m].cpu(), torch.arange(m), torch.zeros(m // 64 * ocw.PAGE_BYTES,
+                                                                               dtype=torch.uint8))
+        got = view[perm[b * ppr:b * ppr + m // 64]].cpu().reshape(-1)
+        ok = ok and torch.equal(got, want)
+    okt = torch.tensor([int(ok)], dtype=torch.int32, device=dev)
+    ms_total, total_bytes, _ = sharding.reduce_step_stats(ms_kernel * K, float(rank_bytes), float(n), world)
+    if world > 1:
+        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+    if rank != 0:
+        barrier()
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+    ms_step = ms_total / K
+    value = total_bytes / (ms_step * 1e-3) / 1e9
+    peak, peak_kind = measured_peaks()
+    per_gpu = value / world
+    cpu = None
+    if world == 1 and args.cpu_seconds > 0:
+        torch.set_num_threads(os.cpu_count() or 1)
+        m = 4096
+        ks = k[:m].cpu()
+        t0 = time.perf_counter()
+        ocw.write_cache(ks, torch.arange(m), torch.zeros(m // 64 * ocw.PAGE_BYTES, dtype=torch.uint8))
+        t = time.perf_counter() - t0
+        cpu = {"value": m * per_tok / t / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+               "kind": "port", "sample": f"cache-writer oracle on {m} tokens, {t * 1e3:.0f} ms"}
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,
+        "tokens_per_s": world * n / (ms_step * 1e-3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, fp8e4m3 + fp32 scale out",
+        "data": "synthetic (seeded N(0,1) keys, random page permutation)",
+        "config": {"workload": "cache_write",
+                   "description": f"{B} requests x {L} tokens per GPU quantised into the paged "
+                                  "FP8 index cache",
+                   "tokens_per_gpu": n, "parallelism": f"dp{world} (each GPU its own cache)",
+                   "l2": f"inputs larger than L2 ({n * 264 / 1e9:.2f} GB read, "
+                         f"{n * 132 / 1e9:.2f} GB written per step), no flush"},
+        "roofline": {"bound": "hbm", "op": "index K-cache writer", "achieved": per_gpu,
+                     "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                     "traffic": profiled_traffic("index_cache_write_kernel", "cache_write")},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": K,
+        "clocks": clk.summary(),
+        "verified": bool(okt.item()),
     }
     print(json.dumps(line), flush=True)
     if world > 1:

@@ -12,10 +12,28 @@
 //   q_d   = e4m3(k_d / scale), round to nearest even
 // Slots < 0 are padding and skipped; slots beyond the cache set a status bit.
 //
-// One warp per token: a lane loads 4 bf16 (8 bytes, coalesced 256 B per
-// warp), the warp max-reduces |k| with shuffles, and each lane writes its 4
-// fp8 bytes; lane 0 writes the scale.  HBM-bound: 256 B read + 132 B written
-// per token.
+// One warp per group of kTokPerWarp consecutive tokens: a lane loads 4 bf16
+// (8 bytes, coalesced 256 B per warp) of every token of the group before it
+// uses any, so a warp keeps 2 KB of keys in flight (64 KB per SM at the 32
+// resident warps that 59 registers a thread allow, four blocks; one token
+// per warp left 16 KB per SM in flight); the warp max-reduces |k| of all the
+// group's tokens with interleaved shuffles, and each lane writes its 4 fp8
+// bytes of every token; lane 0 writes the scales.  256 B of key + 8 B of slot
+// read and 132 B written per token.
+//
+// The kernel is bound by instruction issue, not HBM (a persistent version
+// streaming the keys through shared memory with bulk copies, 128 KB in
+// flight per SM, ran slower), and IEEE division is most of a token's
+// instructions.  k / scale is therefore computed as one correctly rounded
+// reciprocal per token (__frcp_rn) and, per value, Markstein's FMA-corrected
+// quotient (P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990):
+//   q0 = RN(x * r),  e = x - q0 * scale (exact, one FMA),  q = RN(q0 + e * r)
+// which, with r = RN(1 / scale) and no overflow or underflow of the
+// quotient, equals RN(x / scale).  Here |x / scale| <= 448 (scale >= amax/448)
+// and a quotient small enough to be subnormal rounds to an fp8 zero of the
+// same sign either way; the GPU tests check every byte against IEEE
+// division over half a million tokens spanning 40 decades of magnitude.
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
@@ -29,6 +47,8 @@ constexpr int kDim = DSA_INDEX_DIM;                 // 128
 constexpr int kPage = DSA_PAGE_SIZE;                // 64
 constexpr int kPageBytes = DSA_INDEX_PAGE_BYTES;    // 8448
 constexpr int kWarpsPerBlock = 8;
+constexpr int kTokPerWarp = 8;
+constexpr int kTokPerBlock = kWarpsPerBlock * kTokPerWarp;
 
 // 2^ceil(log2(s)) for a positive normal float, exactly: s itself when its
 // mantissa is zero, else the next power of two.
@@ -38,38 +58,66 @@ __device__ __forceinline__ float pow2_ceil(float s) {
   return __uint_as_float((u & 0x7F800000u) + 0x00800000u);
 }
 
-__global__ void __launch_bounds__(32 * kWarpsPerBlock)
+__global__ void __launch_bounds__(32 * kWarpsPerBlock, 4)
 index_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const int64_t* __restrict__ slots,
                          int num_tokens, uint8_t* __restrict__ cache, int64_t num_slots,
                          int ue8m0, unsigned int* status) {
   const int lane = threadIdx.x & 31;
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
-  if (t >= num_tokens) return;
-  const int64_t slot = __ldg(slots + t);
-  if (slot < 0) return;  // padding
-  if (slot >= num_slots) {
-    if (lane == 0 && status != nullptr) atomicOr(status, DSA_DEV_BAD_INDEX);
-    return;
-  }
-  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(k + t * kDim) + lane);
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-  float amax = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y)));
+  const int64_t t0 =
+      (static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5)) * kTokPerWarp;
+  if (t0 >= num_tokens) return;
+  const int n = num_tokens - t0 < kTokPerWarp ? static_cast<int>(num_tokens - t0) : kTokPerWarp;
+  // Lane i < n holds the slot of token t0 + i.
+  const int64_t my_slot = lane < n ? __ldg(slots + t0 + lane) : -1;
+  uint2 raw[kTokPerWarp];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  float scale = fmaxf(1e-4f, amax) / 448.0f;
-  if (ue8m0) scale = pow2_ceil(scale);
-  const float v[4] = {a.x / scale, a.y / scale, b.x / scale, b.y / scale};
-  uint32_t packed = 0;
+  for (int i = 0; i < kTokPerWarp; ++i)
+    raw[i] = i < n ? __ldg(reinterpret_cast<const uint2*>(k + (t0 + i) * kDim) + lane)
+                   : make_uint2(0u, 0u);
+  float amax[kTokPerWarp];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __nv_fp8_storage_t q = __nv_cvt_float_to_fp8(v[i], __NV_SATFINITE, __NV_E4M3);
-    packed |= static_cast<uint32_t>(q) << (8 * i);
+  for (int i = 0; i < kTokPerWarp; ++i) {
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].y));
+    amax[i] = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y)));
   }
-  uint8_t* page = cache + (slot / kPage) * kPageBytes;
-  const int tok = static_cast<int>(slot % kPage);
-  *reinterpret_cast<uint32_t*>(page + tok * kDim + 4 * lane) = packed;
-  if (lane == 0) *reinterpret_cast<float*>(page + kPage * kDim + 4 * tok) = scale;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int i = 0; i < kTokPerWarp; ++i)
+      amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], o));
+  }
+#pragma unroll
+  for (int i = 0; i < kTokPerWarp; ++i) {
+    const int64_t slot = __shfl_sync(0xffffffffu, my_slot, i);
+    if (i >= n || slot < 0) continue;  // past the end, or padding
+    if (slot >= num_slots) {
+      if (lane == 0 && status != nullptr) atomicOr(status, DSA_DEV_BAD_INDEX);
+      continue;
+    }
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].y));
+    float scale = fmaxf(1e-4f, amax[i]) / 448.0f;
+    if (ue8m0) scale = pow2_ceil(scale);
+    const float r = __frcp_rn(scale);
+    const float x[4] = {a.x, a.y, b.x, b.y};
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float q0 = __fmul_rn(x[j], r);
+      v[j] = __fmaf_rn(__fmaf_rn(-q0, scale, x[j]), r, q0);
+    }
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_fp8_storage_t q = __nv_cvt_float_to_fp8(v[j], __NV_SATFINITE, __NV_E4M3);
+      packed |= static_cast<uint32_t>(q) << (8 * j);
+    }
+    uint8_t* page = cache + (slot / kPage) * kPageBytes;
+    const int tok = static_cast<int>(slot % kPage);
+    *reinterpret_cast<uint32_t*>(page + tok * kDim + 4 * lane) = packed;
+    if (lane == 0) *reinterpret_cast<float*>(page + kPage * kDim + 4 * tok) = scale;
+  }
 }
 
 }  // namespace kc
@@ -90,8 +138,8 @@ extern "C" int dsa_index_cache_write(const void* k, const int64_t* slot_mapping,
   DeviceInfo info;
   const int st = current_device_info(&info);
   if (st != DSA_OK) return st;
-  const int blocks = (num_tokens + kc::kWarpsPerBlock - 1) / kc::kWarpsPerBlock;
-  kc::index_cache_write_kernel<<<blocks, 32 * kc::kWarpsPerBlock, 0,
+  const int64_t blocks = (static_cast<int64_t>(num_tokens) + kc::kTokPerBlock - 1) / kc::kTokPerBlock;
+  kc::index_cache_write_kernel<<<static_cast<unsigned int>(blocks), 32 * kc::kWarpsPerBlock, 0,
                                  reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(k), slot_mapping, num_tokens,
       static_cast<uint8_t*>(k_index_cache_fp8), num_pages * kc::kPage, ue8m0 != 0,

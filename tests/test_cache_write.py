@@ -87,6 +87,31 @@ def test_gpu_matches_oracle_bit_exact(cuda_device, ue8m0):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("ue8m0", [False, True])
+def test_gpu_quotients_match_ieee_division(cuda_device, ue8m0):
+    """The kernel forms k / scale with a reciprocal and an FMA correction;
+    every byte must equal IEEE division followed by the e4m3 conversion (the
+    oracle's quantize on the CPU: on the GPU torch divides by a Python scalar
+    as a multiplication by its reciprocal, which is not IEEE division), over
+    half a million tokens whose rows span 40 decades and whose values span 6
+    decades in a row."""
+    from dsa_b200 import cache as kc
+
+    n = 1 << 19
+    g = torch.Generator(device=cuda_device).manual_seed(11)
+    rows = torch.pow(10.0, torch.empty(n, 1, device=cuda_device).uniform_(-20, 20, generator=g))
+    spread = torch.pow(10.0, torch.empty(n, 128, device=cuda_device).uniform_(-6, 0, generator=g))
+    k = (torch.randn(n, 128, generator=g, device=cuda_device) * rows * spread).to(torch.bfloat16)
+    cache = torch.zeros(n // 64 * ocw.PAGE_BYTES, dtype=torch.uint8, device=cuda_device)
+    kc.write_index_k(k, torch.arange(n, device=cuda_device), cache, ue8m0=ue8m0)
+    q, scale = ocw.quantize(k.cpu(), ue8m0)
+    want = torch.cat([q.reshape(n // 64, 64 * 128),
+                      scale.contiguous().view(torch.uint8).reshape(n // 64, 64 * 4)], dim=1).reshape(-1)
+    bad = (cache.cpu() != want).nonzero()
+    assert bad.numel() == 0, f"{bad.numel()} bytes differ, first at {bad[:4].flatten().tolist()}"
+
+
+@pytest.mark.gpu
 def test_gpu_out_of_range_slot_is_reported_not_written(cuda_device):
     lib = _native.lib()
     k = _keys(3, 6).to(cuda_device)
