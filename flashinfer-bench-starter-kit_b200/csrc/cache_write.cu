@@ -19,7 +19,9 @@
 // per warp left 16 KB per SM in flight); the warp max-reduces |k| of all the
 // group's tokens with interleaved shuffles, and each lane writes its 4 fp8
 // bytes of every token; lane 0 writes the scales.  256 B of key + 8 B of slot
-// read and 132 B written per token.
+// read and 132 B written per token.  The maxima are reduce-scattered so that
+// each lane ends with one token's maximum and computes that token's scale and
+// reciprocal: one division and one reciprocal per lane, not one per token.
 //
 // The kernel is bound by instruction issue, not HBM (a persistent version
 // streaming the keys through shared memory with bulk copies, 128 KB in
@@ -81,15 +83,36 @@ index_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const int64_t* __r
     const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].y));
     amax[i] = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y)));
   }
+  // Reduce-scatter of the eight maxima: at each of the steps xor 16, 8, 4 a
+  // lane keeps half of its partial maxima (chosen by its lane bit) and sends
+  // the other half to its partner, so afterwards lane l holds the maximum
+  // over lanes l ^ {0, 4, ..., 28} of token l >> 2; two plain butterfly steps
+  // finish it.  max is exact and order-independent.
+  const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+  float a4[4], a2[2];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-    for (int i = 0; i < kTokPerWarp; ++i)
-      amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], o));
+  for (int j = 0; j < 4; ++j) {
+    const float send = b4 ? amax[j] : amax[j + 4];
+    a4[j] = fmaxf(b4 ? amax[j + 4] : amax[j], __shfl_xor_sync(0xffffffffu, send, 16));
   }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float send = b3 ? a4[j] : a4[j + 2];
+    a2[j] = fmaxf(b3 ? a4[j + 2] : a4[j], __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+  float a1 = fmaxf(b2 ? a2[1] : a2[0], __shfl_xor_sync(0xffffffffu, b2 ? a2[0] : a2[1], 4));
+  a1 = fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, 2));
+  a1 = fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+  // Scale and its correctly rounded reciprocal of token lane >> 2, once per
+  // lane instead of once per lane and token.
+  float my_scale = fmaxf(1e-4f, a1) / 448.0f;
+  if (ue8m0) my_scale = pow2_ceil(my_scale);
+  const float my_rcp = __frcp_rn(my_scale);
 #pragma unroll
   for (int i = 0; i < kTokPerWarp; ++i) {
     const int64_t slot = __shfl_sync(0xffffffffu, my_slot, i);
+    const float scale = __shfl_sync(0xffffffffu, my_scale, 4 * i);
+    const float r = __shfl_sync(0xffffffffu, my_rcp, 4 * i);
     if (i >= n || slot < 0) continue;  // past the end, or padding
     if (slot >= num_slots) {
       if (lane == 0 && status != nullptr) atomicOr(status, DSA_DEV_BAD_INDEX);
@@ -97,9 +120,6 @@ index_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const int64_t* __r
     }
     const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].x));
     const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].y));
-    float scale = fmaxf(1e-4f, amax[i]) / 448.0f;
-    if (ue8m0) scale = pow2_ceil(scale);
-    const float r = __frcp_rn(scale);
     const float x[4] = {a.x, a.y, b.x, b.y};
     float v[4];
 #pragma unroll
@@ -107,15 +127,13 @@ index_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const int64_t* __r
       const float q0 = __fmul_rn(x[j], r);
       v[j] = __fmaf_rn(__fmaf_rn(-q0, scale, x[j]), r, q0);
     }
-    uint32_t packed = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __nv_fp8_storage_t q = __nv_cvt_float_to_fp8(v[j], __NV_SATFINITE, __NV_E4M3);
-      packed |= static_cast<uint32_t>(q) << (8 * j);
-    }
+    // Pairs convert in one instruction (round to nearest even, saturating;
+    // the first element lands in the low byte).
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v[0], v[1]), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v[2], v[3]), __NV_SATFINITE, __NV_E4M3);
     uint8_t* page = cache + (slot / kPage) * kPageBytes;
     const int tok = static_cast<int>(slot % kPage);
-    *reinterpret_cast<uint32_t*>(page + tok * kDim + 4 * lane) = packed;
+    *reinterpret_cast<uint32_t*>(page + tok * kDim + 4 * lane) = lo | (hi << 16);
     if (lane == 0) *reinterpret_cast<float*>(page + kPage * kDim + 4 * tok) = scale;
   }
 }
