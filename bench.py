@@ -661,7 +661,7 @@ def run_config3(args, rank: int, world: int, local_rank: int) -> int:
 
 def run_cache_write(args, rank: int, world: int, local_rank: int) -> int:
     """Indexer K-cache population: B requests x L tokens per GPU (default 64 x
-    65536, the cache the north-star indexer reads) quantised into the paged
+    65536, the cache the default decode workload's indexer reads) quantised into the paged
     FP8 cache, one dsa_index_cache_write launch per step, captured as a CUDA
     graph.  Algorithmic bytes per token: 256 B of bf16 key + 8 B of slot read,
     128 B of FP8 row + 4 B of scale written.  Each GPU writes its own cache
