@@ -17,16 +17,19 @@
 // uses any, so a warp keeps 2 KB of keys in flight (80 KB per SM at the 40
 // resident warps of five blocks, 48 registers a thread: 5 % faster than four
 // blocks, while six spill; one token per warp left 16 KB per SM in flight);
-// the warp max-reduces |k| of all the group's tokens, and each lane writes its 4 fp8
-// bytes of every token; lane 0 writes the scales.  256 B of key + 8 B of slot
-// read and 132 B written per token.  The maxima are reduce-scattered so that
-// each lane ends with one token's maximum and computes that token's scale and
-// reciprocal: one division and one reciprocal per lane, not one per token.
+// the warp max-reduces |k| of all the group's tokens, and each lane writes
+// its 4 fp8 bytes of every token.  256 B of key + 8 B of slot read and 132 B
+// written per token.  The maxima are reduce-scattered so that the lanes of
+// token i (lanes 4i..4i+3) end with its maximum and compute its scale and
+// reciprocal, resolve its slot (row address, validity) and, the first of
+// them, store its scale: per lane one division, one reciprocal and one slot,
+// not one per token.
 //
-// The kernel is bound by instruction issue, not HBM (a persistent version
-// streaming the keys through shared memory with bulk copies, 128 KB in
-// flight per SM, ran slower), and IEEE division is most of a token's
-// instructions.  k / scale is therefore computed as one correctly rounded
+// Instruction issue, not memory latency, bounded the first versions (a
+// persistent kernel streaming the keys through shared memory with bulk
+// copies, 128 KB in flight per SM, ran slower), and IEEE division was most
+// of a token's instructions; with the steps below the kernel runs at the
+// HBM bound.  k / scale is therefore computed as one correctly rounded
 // reciprocal per token (__frcp_rn) and, per value, Markstein's FMA-corrected
 // quotient (P. Markstein, "Computation of elementary functions on the IBM
 // RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990):
@@ -75,8 +78,10 @@ index_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const int64_t* __r
       (static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5)) * kTokPerWarp;
   if (t0 >= num_tokens) return;
   const int n = num_tokens - t0 < kTokPerWarp ? static_cast<int>(num_tokens - t0) : kTokPerWarp;
-  // Lane i < n holds the slot of token t0 + i.
-  const int64_t my_slot = lane < n ? __ldg(slots + t0 + lane) : -1;
+  // Lane l holds the slot of token t0 + l / kLanesPerTok (the lanes of one
+  // token load the same word).
+  const int my_tok = lane / kLanesPerTok;
+  const int64_t my_slot = my_tok < n ? __ldg(slots + t0 + my_tok) : -1;
   uint2 raw[kTokPerWarp];
 #pragma unroll
   for (int i = 0; i < kTokPerWarp; ++i)
@@ -117,16 +122,25 @@ index_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const int64_t* __r
   float my_scale = fmaxf(1e-4f, a1) / 448.0f;
   if (ue8m0) my_scale = pow2_ceil(my_scale);
   const float my_rcp = __frcp_rn(my_scale);
+  // The token's slot is resolved once, by its lanes: validity (negative =
+  // padding, skipped; beyond the cache = reported, skipped), its row address,
+  // and the scale, which the token's first lane stores.
+  const bool lead = (lane % kLanesPerTok) == 0;
+  const bool valid = my_slot >= 0 && my_slot < num_slots;
+  if (lead && my_slot >= num_slots && status != nullptr) atomicOr(status, DSA_DEV_BAD_INDEX);
+  const int64_t my_page = valid ? my_slot / kPage : 0;
+  const int my_row = valid ? static_cast<int>(my_slot % kPage) : 0;
+  uint8_t* page = cache + my_page * kPageBytes;
+  if (lead && valid) *reinterpret_cast<float*>(page + kPage * kDim + 4 * my_row) = my_scale;
+  const unsigned long long my_rowp = reinterpret_cast<unsigned long long>(page + my_row * kDim);
+  const unsigned int vmask = __ballot_sync(0xffffffffu, valid);
 #pragma unroll
   for (int i = 0; i < kTokPerWarp; ++i) {
-    const int64_t slot = __shfl_sync(0xffffffffu, my_slot, i);
-    const float scale = __shfl_sync(0xffffffffu, my_scale, kLanesPerTok * i);
-    const float r = __shfl_sync(0xffffffffu, my_rcp, kLanesPerTok * i);
-    if (i >= n || slot < 0) continue;  // past the end, or padding
-    if (slot >= num_slots) {
-      if (lane == 0 && status != nullptr) atomicOr(status, DSA_DEV_BAD_INDEX);
-      continue;
-    }
+    const int src = kLanesPerTok * i;
+    const float scale = __shfl_sync(0xffffffffu, my_scale, src);
+    const float r = __shfl_sync(0xffffffffu, my_rcp, src);
+    const unsigned long long rowp = __shfl_sync(0xffffffffu, my_rowp, src);
+    if (!((vmask >> src) & 1u)) continue;  // past the end, padding or out of range
     const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].x));
     const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].y));
     const float x[4] = {a.x, a.y, b.x, b.y};
@@ -140,10 +154,7 @@ index_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const int64_t* __r
     // the first element lands in the low byte).
     const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v[0], v[1]), __NV_SATFINITE, __NV_E4M3);
     const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v[2], v[3]), __NV_SATFINITE, __NV_E4M3);
-    uint8_t* page = cache + (slot / kPage) * kPageBytes;
-    const int tok = static_cast<int>(slot % kPage);
-    *reinterpret_cast<uint32_t*>(page + tok * kDim + 4 * lane) = lo | (hi << 16);
-    if (lane == 0) *reinterpret_cast<float*>(page + kPage * kDim + 4 * tok) = scale;
+    reinterpret_cast<uint32_t*>(rowp)[lane] = lo | (hi << 16);
   }
 }
 
