@@ -31,16 +31,21 @@
 //     warps 0-3  online softmax in base 2 with lazy rescaling (the running
 //                max is only moved when a tile exceeds it by more than 8,
 //                so O in TMEM is rarely touched), P^T written as bf16.
-//   A token fully covered by one CTA is normalised and written directly;
-//   otherwise each covering CTA writes a partial (O / l in bf16, m, l) and
-//   bumps a per-token counter; the last one to arrive merges them once its
-//   own tiles are done, with all of its threads:
+//   A token fully covered by one CTA is normalised and written directly.
+//   Otherwise each covering CTA takes a ticket from the token's arrival
+//   counter when its segment ends.  Every CTA but the last to arrive writes
+//   its partial (O in fp32, m, l) and then bumps the token's publication
+//   counter; the last one waits until the others have published -- they
+//   have all arrived already, so the wait is short and cannot depend on a
+//   CTA that is not running -- and merges them with its own accumulator
+//   straight from TMEM, without storing its own part:
 //   lse = log2 L + M with L = sum_i l_i 2^(m_i - M),
-//   out = sum_i (O_i / l_i) l_i 2^(m_i - M) / L.
+//   out = sum_i O_i 2^(m_i - M) / L.
 //   The counters sit at the end of the workspace; the merging CTA resets its
-//   token's counter, so they are zero between calls (no memset).
+//   token's counters, so they are zero between calls (no memset).
 #include <cuda_bf16.h>
 
+#include <atomic>
 #include <cmath>
 #include <mutex>
 
@@ -73,10 +78,17 @@ constexpr uint32_t kColO = 0;    // O^T buffers at [0,64) and [64,128): 4 blocks
 constexpr uint32_t kColS = 128;  // S^T buffers at [128,192) and [192,256): 4 partial sums x 16 heads
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: factor 256
 constexpr int kMaxTokens = (1 << 30) / (kTopK / kRows) / kHeads;
-// Most partial records a token can have (its 32 tiles meet at most 33 CTA
-// slices); the merge scratch holds two [kMaxParts][16] float arrays and the
-// parts' record indices.
+// Most parts a token can have (its 32 tiles meet at most 33 CTA slices); the
+// merge scratch holds the parts' per-head weights ([kMaxParts][16] floats)
+// and record indices.
 constexpr int kMaxParts = 48;
+// A partial record: the part's O^T, [4 column blocks][128 dims][16 heads]
+// fp32 -- the order in which the 128 softmax threads hold it (thread e: dims
+// 128 mb + e, all heads), so each thread moves 64 contiguous bytes per block.
+constexpr int kPartFloats = 4 * 128 * kHeads;  // 8192 floats = 32 KiB
+// Only a CTA's first and last token segments can be partial: two records
+// per CTA, slot 0 for its first segment and slot 1 for its last.
+constexpr int kRecsPerCta = 2;
 
 // bf16 x bf16 -> f32.  Logits: A = K rows (K-major), B = Q (K-major), M64 N16.
 constexpr uint32_t kIdescS = idesc_make(1, 1, false, false, 64, 16);
@@ -90,10 +102,16 @@ constexpr int kOffSx = kOffP + 2 * kPBytes;          // 188416
 constexpr int kOffBar = kOffSx + kHeads * kRows * 4; // 192512
 constexpr int kOffMisc = kOffBar + 256;
 constexpr int kSmemBytes = 1024 + kOffMisc + 256;
-static_assert((18 + kMmaWarps) * 8 <= 256, "barrier area");
+static_assert((18 + kMmaWarps + 1) * 8 <= 256, "barrier area");
 static_assert(kOffSx == kOffP + 2 * kPBytes &&
-                  2 * kPBytes + kHeads * kRows * 4 >= 2 * kMaxParts * kHeads * 4 + kMaxParts * 8,
+                  2 * kPBytes + kHeads * kRows * 4 >= (kMaxParts + 1) * kHeads * 4 + kMaxParts * 8,
               "merge scratch: the P and Sx buffers, contiguous");
+
+// Test-only fault injection (dsa_b200_test_inject): the producer group of
+// each CTA's second tile issues no copy and no arrival for it, so the MMA
+// issuers' wait on that tile runs out and the CTA aborts.
+constexpr int kInjectNone = 0;
+constexpr int kInjectSkipArrival = DSA_TEST_SKIP_ARRIVAL;
 
 struct Params {
   const int32_t* indices;
@@ -101,14 +119,16 @@ struct Params {
   const uint8_t* kpe;      // [num_slots][64] bf16
   __nv_bfloat16* out;
   float* lse;
-  __nv_bfloat16* part_o;  // [records][16][512]: the part's O / l
-  float* part_ml;         // [records][16][2]: the part's (m, l)
-  int* tok_count;  // [num_tokens] partials written so far; zero between calls (the merging CTA resets it)
+  float* part_o;   // [grid * 2][kPartFloats]: a part's O^T (not normalised)
+  float* part_ml;  // [grid * 2][16][2]: the part's (m, l)
+  int* tok_arrive;  // [num_tokens] tickets taken; zero between calls (the merging CTA resets it)
+  int* tok_pub;     // [num_tokens] partials published; likewise
   unsigned int* status;
   int64_t num_slots;
   int num_tokens;
-  int kmax;        // partial records per CTA
   float scale_log2;
+  unsigned long long wait_limit_ns;  // kWaitLimitNs unless a test shortened it
+  int inject;                        // kInjectNone unless a test asked for a fault
 };
 
 // Which tokens / records a CTA covers, shared by both kernels.
@@ -138,105 +158,194 @@ __device__ __forceinline__ int parts_of(int t, int64_t total, int grid) {
   return hi - lo + 1;
 }
 
-// Merges the (O, m, l) partials of token t.  Run by all kThreads threads of
-// the CTA that wrote the token's last partial, after its own work is done;
-// sm: 2 * kMaxParts * 16 floats of shared memory.  The per-part (m, l) loads
-// are all in flight together, and each thread keeps four parts' 16 output
-// columns in flight per round, so a token costs about ceil(parts / 4) + 1
-// L2 round trips:
-//   lse = log2 L + M with L = sum_i l_i 2^(m_i - M), out = sum_i (O_i / l_i) l_i 2^(m_i - M) / L
-// (parts are stored normalised, O_i / l_i, in bf16).
-__device__ void merge_token(const Params& p, int t, int64_t total, int grid, float* sm) {
+// Record of CTA c's part of token t: slot 0 if t is c's first token
+// segment, else slot 1 (its last).
+__device__ __forceinline__ int64_t part_record(int t, int c, int64_t total, int grid) {
+  const int tf = static_cast<int>(unit_start(total, c, grid) / kTilesPerTok);
+  return static_cast<int64_t>(c) * kRecsPerCta + (t == tf ? 0 : 1);
+}
+
+// A token of up to this many parts whose last part is its CTA's last
+// segment is merged by that CTA's softmax threads as soon as the segment
+// ends, its own part read straight from TMEM.  Otherwise (many parts, at
+// small token counts where CTAs hold few tiles, or a last part that is the
+// CTA's first segment) every part is published as a record and the last
+// arriver merges them with all of its threads once its own tiles are done.
+constexpr int kInlineParts = 4;
+
+// Per-head merge weights of token t's parts, by threads e < 16 (head e):
+// wts[i][e] = 2^(m_i - M) / L for parts i = 0 .. nparts-1 in CTA order,
+// lse = M + log2 L.  Part i's (m, l) come from its record, except for the
+// caller's own part (recs[i] < 0), whose (m, l) per head are own_ml.  The
+// sums run in part order whichever CTA merges, so a call's result does not
+// depend on which CTA arrived last.
+__device__ __forceinline__ void merge_weights(const Params& p, int t, int nparts, const int64_t* recs,
+                                              const float* own_ml, float* wts, int e) {
+  float M = -INFINITY;
+  for (int i = 0; i < nparts; ++i) {
+    const float m = recs[i] < 0 ? own_ml[2 * e] : __ldcg(p.part_ml + recs[i] * 2 * kHeads + 2 * e);
+    wts[i * kHeads + e] = m;
+    M = fmaxf(M, m);
+  }
+  float L = 0.f;
+  for (int i = 0; i < nparts; ++i) {
+    const float m = wts[i * kHeads + e];
+    const float w = m == -INFINITY ? 0.f : exp2f(m - M);
+    const float l = recs[i] < 0 ? own_ml[2 * e + 1] : __ldcg(p.part_ml + recs[i] * 2 * kHeads + 2 * e + 1);
+    L += l * w;
+    wts[i * kHeads + e] = w;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  for (int i = 0; i < nparts; ++i) wts[i * kHeads + e] *= inv;
+  p.lse[static_cast<int64_t>(t) * kHeads + e] = L > 0.f ? M + log2f(L) : -INFINITY;
+}
+
+// Writes 16 heads of output dim `dim` of token t (bf16).
+__device__ __forceinline__ void store_out_column(const Params& p, int t, int dim, const float (&acc)[16]) {
+  __nv_bfloat16* out = p.out + static_cast<int64_t>(t) * kHeads * kCkv + dim;
+#pragma unroll
+  for (int hh = 0; hh < kHeads; ++hh) out[hh * kCkv] = __float2bfloat16_rn(acc[hh]);
+}
+
+// Every wait on a publication counter is bounded by twice the pipeline
+// limit: a CTA that holds a ticket publishes (or settles, after an abort) at
+// most one pipeline wait later, so a waiter never gives up on a part that
+// is still coming.
+
+// Inline merge by the 128 softmax threads of the CTA holding token t's last
+// part (nparts <= kInlineParts), at the end of the CTA's last segment: its
+// own O^T is in TMEM at `obuf` (this thread's lanes), its (m, l) per head in
+// own_ml; the other parts are records.  Each thread copies its 64 bytes per
+// column block of every other record into `landing` (the idle K/V stage
+// ring) with cp.async, all in flight together and overlapping the (m, l)
+// loads of the weights, then combines them with its TMEM accumulator.
+// scratch: (kMaxParts + 1) * 16 floats + kMaxParts int64.
+__device__ __forceinline__ void merge_inline(const Params& p, int t, int64_t total, int grid, uint32_t obuf,
+                                             const float* own_ml, float* scratch, uint8_t* landing, int e) {
+  int c_lo, c_hi;
+  covering_ctas(t, total, grid, c_lo, c_hi);
+  const int nparts = c_hi - c_lo + 1;
+  float* wts = scratch;
+  int64_t* recs = reinterpret_cast<int64_t*>(scratch + (kMaxParts + 1) * kHeads);
+  if (e < nparts) {
+    const int c = c_lo + e;
+    recs[e] = c == static_cast<int>(blockIdx.x) ? -1 : part_record(t, c, total, grid);
+  }
+  bool ok = true;
+  if (e == 0) ok = wait_counter_at_least(p.tok_pub + t, nparts - 1, p.status, 2 * p.wait_limit_ns);
+  if (named_barrier_and(1, 128, ok)) {
+    const uint32_t land = smem_u32(landing);
+    const uint64_t policy = make_policy_evict_first();
+    for (int i = 0; i < nparts; ++i) {
+      if (recs[i] < 0) continue;
+      const float* src = p.part_o + recs[i] * kPartFloats + e * kHeads;
+#pragma unroll
+      for (int mb = 0; mb < 4; ++mb)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          cp_async16(land + (((i * 4 + mb) * 128 + e) * 4 + q) * 16, src + mb * 128 * kHeads + 4 * q, policy);
+    }
+    if (e < kHeads) merge_weights(p, t, nparts, recs, own_ml, wts, e);
+    cp_async_wait_all();  // this thread's own copies; it alone reads them
+    named_barrier_sync(1, 128);
+#pragma unroll 1
+    for (int mb = 0; mb < 4; ++mb) {
+      float own[16], acc[16];
+      tmem_ld16(obuf + 16 * mb, own);
+      tmem_wait_ld();
+#pragma unroll
+      for (int hh = 0; hh < kHeads; ++hh) acc[hh] = 0.f;
+      for (int i = 0; i < nparts; ++i) {  // part order: the same sums whoever merges
+        const float* wv = wts + i * kHeads;
+        if (recs[i] < 0) {
+#pragma unroll
+          for (int hh = 0; hh < kHeads; ++hh) acc[hh] = fmaf(own[hh], wv[hh], acc[hh]);
+        } else {
+          const float4* f = reinterpret_cast<const float4*>(landing + (((i * 4 + mb) * 128 + e) * 4) * 16);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 x = f[q];
+            acc[4 * q] = fmaf(x.x, wv[4 * q], acc[4 * q]);
+            acc[4 * q + 1] = fmaf(x.y, wv[4 * q + 1], acc[4 * q + 1]);
+            acc[4 * q + 2] = fmaf(x.z, wv[4 * q + 2], acc[4 * q + 2]);
+            acc[4 * q + 3] = fmaf(x.w, wv[4 * q + 3], acc[4 * q + 3]);
+          }
+        }
+      }
+      store_out_column(p, t, 128 * mb + e, acc);
+    }
+  }
+  if (e == 0) {  // the token's counters are zero again for the next call
+    p.tok_arrive[t] = 0;
+    p.tok_pub[t] = 0;
+  }
+}
+
+// Deferred merge of token t (nparts > kInlineParts) from every part's record,
+// by all kThreads threads of the last arriver once its own work is done.
+// Thread -> float4 j = tid + 512 q (q < 4) of each 2048-float4 record, i.e.
+// dims 128 mb + e and heads 4 g .. 4 g + 3 with j = (mb * 128 + e) * 4 + g;
+// four parts' loads are in flight per round.  sm: as merge_inline's scratch.
+__device__ __forceinline__ void merge_deferred(const Params& p, int t, int64_t total, int grid, float* sm) {
   const int tid = threadIdx.x;
   int c_lo, c_hi;
   covering_ctas(t, total, grid, c_lo, c_hi);
   const int nparts = c_hi - c_lo + 1;
+  float* wts = sm;
+  int64_t* recs = reinterpret_cast<int64_t*>(sm + (kMaxParts + 1) * kHeads);
   if (nparts > kMaxParts) {  // cannot happen for grids of <= 2^20 CTAs; never read past sm
     if (tid == 0) atomicOr(p.status, DSA_DEV_BAD_INDEX);
     return;
   }
-  float* mw = sm;                      // m_i[h], then the weight 2^(m_i - M) / l
-  float* lv = sm + kMaxParts * kHeads; // l_i[h]
-  int64_t* recs = reinterpret_cast<int64_t*>(sm + 2 * kMaxParts * kHeads);
-  if (tid < nparts) {
-    const int c = c_lo + tid;
-    recs[tid] = static_cast<int64_t>(c) * p.kmax +
-                (t - static_cast<int>(unit_start(total, c, grid) / kTilesPerTok));
-  }
+  if (tid < nparts) recs[tid] = part_record(t, c_lo + tid, total, grid);
+  int* flag = reinterpret_cast<int*>(recs + kMaxParts);
+  if (tid == 0) *flag = wait_counter_at_least(p.tok_pub + t, nparts, p.status, 2 * p.wait_limit_ns) ? 1 : 0;
   __syncthreads();
-  // Thread -> head tid / 32, 16 consecutive columns: a warp reads 2 KB
-  // contiguous per part.  The first four parts' columns and every part's
-  // (m, l) are requested together, so the weights below are computed while
-  // the column loads are in flight.
-  const int h = tid >> 5;
-  const int c0 = (tid & 31) * 16;
-  auto load4 = [&](int i0, uint4 (&v)[4][2]) {
+  if (*flag) {
+    if (tid < kHeads) merge_weights(p, t, nparts, recs, nullptr, wts, tid);
+    __syncthreads();
+    float acc[4][4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      v[k][0] = v[k][1] = make_uint4(0u, 0u, 0u, 0u);
-      if (i0 + k < nparts) {
-        const uint4* src =
-            reinterpret_cast<const uint4*>(p.part_o + (recs[i0 + k] * kHeads + h) * kCkv + c0);
-        v[k][0] = __ldcg(src);
-        v[k][1] = __ldcg(src + 1);
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[q][k] = 0.f;
+    for (int i0 = 0; i0 < nparts; i0 += 4) {
+      float4 v[4][4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (i0 + k < nparts) {
+          const float4* src = reinterpret_cast<const float4*>(p.part_o + recs[i0 + k] * kPartFloats);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v[k][q] = __ldcg(src + tid + 512 * q);
+        }
       }
-    }
-  };
-  uint4 v[4][2];
-  load4(0, v);
-  for (int idx = tid; idx < nparts * kHeads; idx += kThreads) {
-    const int hh = idx & 15;
-    const int64_t rec = recs[idx >> 4];
-    mw[idx] = __ldcg(p.part_ml + rec * 2 * kHeads + 2 * hh);
-    lv[idx] = __ldcg(p.part_ml + rec * 2 * kHeads + 2 * hh + 1);
-  }
-  __syncthreads();
-  if (tid < kHeads) {
-    float M = -INFINITY;
-    for (int i = 0; i < nparts; ++i) M = fmaxf(M, mw[i * kHeads + tid]);
-    float l = 0.f;
-    for (int i = 0; i < nparts; ++i) {
-      const float mi = mw[i * kHeads + tid];
-      const float w = mi == -INFINITY ? 0.f : lv[i * kHeads + tid] * exp2f(mi - M);
-      l += w;
-      mw[i * kHeads + tid] = w;  // the parts hold O_i / l_i
-    }
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    for (int i = 0; i < nparts; ++i) mw[i * kHeads + tid] *= inv;
-    p.lse[static_cast<int64_t>(t) * kHeads + tid] = l > 0.f ? M + log2f(l) : -INFINITY;
-  }
-  __syncthreads();
-  float acc[16];
 #pragma unroll
-  for (int k = 0; k < 16; ++k) acc[k] = 0.f;
-  for (int i0 = 0; i0 < nparts; i0 += 4) {
-    if (i0 > 0) load4(i0, v);
+      for (int k = 0; k < 4; ++k) {
+        if (i0 + k < nparts) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float w = i0 + k < nparts ? mw[(i0 + k) * kHeads + h] : 0.f;
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const uint32_t wd[4] = {v[k][q].x, v[k][q].y, v[k][q].z, v[k][q].w};
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wd[r]));
-          acc[8 * q + 2 * r] += f.x * w;
-          acc[8 * q + 2 * r + 1] += f.y * w;
+          for (int q = 0; q < 4; ++q) {
+            const float* wv = wts + (i0 + k) * kHeads + 4 * ((tid + 512 * q) & 3);
+            acc[q][0] = fmaf(v[k][q].x, wv[0], acc[q][0]);
+            acc[q][1] = fmaf(v[k][q].y, wv[1], acc[q][1]);
+            acc[q][2] = fmaf(v[k][q].z, wv[2], acc[q][2]);
+            acc[q][3] = fmaf(v[k][q].w, wv[3], acc[q][3]);
+          }
         }
       }
     }
-  }
-  __nv_bfloat16* out = p.out + (static_cast<int64_t>(t) * kHeads + h) * kCkv + c0;
 #pragma unroll
-  for (int k = 0; k < 16; k += 8) {
-    __nv_bfloat162 a0 = __floats2bfloat162_rn(acc[k], acc[k + 1]);
-    __nv_bfloat162 a1 = __floats2bfloat162_rn(acc[k + 2], acc[k + 3]);
-    __nv_bfloat162 a2 = __floats2bfloat162_rn(acc[k + 4], acc[k + 5]);
-    __nv_bfloat162 a3 = __floats2bfloat162_rn(acc[k + 6], acc[k + 7]);
-    uint4 pk;
-    pk.x = *reinterpret_cast<uint32_t*>(&a0); pk.y = *reinterpret_cast<uint32_t*>(&a1);
-    pk.z = *reinterpret_cast<uint32_t*>(&a2); pk.w = *reinterpret_cast<uint32_t*>(&a3);
-    *reinterpret_cast<uint4*>(out + k) = pk;
+    for (int q = 0; q < 4; ++q) {
+      const int j = tid + 512 * q;
+      const int g = j & 3, de = j >> 2;  // de = mb * 128 + e
+      const int dim = de;                 // dims 128 mb + e, in order
+      __nv_bfloat16* out = p.out + static_cast<int64_t>(t) * kHeads * kCkv + dim;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) out[(4 * g + k) * kCkv] = __float2bfloat16_rn(acc[q][k]);
+    }
+  }
+  if (tid == 0) {
+    p.tok_arrive[t] = 0;
+    p.tok_pub[t] = 0;
   }
 }
 
@@ -271,10 +380,13 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   uint64_t* p_empty = bars + 14;
   uint64_t* o_empty = bars + 16;
   uint64_t* drain = bars + 18;  // one per MMA warp
+  // Single-use: completes when the CTA's first tile has landed (group 0).
+  uint64_t* first_full = bars + 18 + kMmaWarps;
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + kOffMisc + 4);
   int* rescale_flag = reinterpret_cast<int*>(smem + kOffMisc + 8);
   int* merge_list = reinterpret_cast<int*>(smem + kOffMisc + 12);  // count, then <= 2 tokens
+  int* ticket_smem = reinterpret_cast<int*>(smem + kOffMisc + 24);
   int* q_last = reinterpret_cast<int*>(smem + kOffMisc + 32);      // last segment loaded per Q slot
   float* alpha_smem = reinterpret_cast<float*>(smem + kOffMisc + 64);   // 16
   float* ml_smem = reinterpret_cast<float*>(smem + kOffMisc + 128);     // 16 x (m, l)
@@ -292,6 +404,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
       mbar_init(&o_empty[s], 1);
     }
     for (int w = 0; w < kMmaWarps; ++w) mbar_init(&drain[w], 1);
+    mbar_init(first_full, 32 * kProdWarps / 2);
     *abort_flag = 0;
     *rescale_flag = 0;
     merge_list[0] = 0;
@@ -316,7 +429,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   const int64_t u1 = unit_start(total, blockIdx.x + 1, gridDim.x);
   const int n = static_cast<int>(u1 - u0);
   const int t_first = static_cast<int>(u0 / kTilesPerTok);
-  const WaitCtx wctx{abort_flag, p.status};
+  const WaitCtx wctx{abort_flag, p.status, p.wait_limit_ns};
 
   if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
     // ------------------------------------------------------ producer warps
@@ -378,19 +491,27 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
       }
       const int s = g;
       if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, wctx))) break;
+      // The second tile's rows are requested only once the first tile's have
+      // landed: with every SM starting at once, the first tile then arrives
+      // in about half the time and the MMA / softmax chain starts earlier.
+      if (i == 1 && !__all_sync(0xffffffffu, mbar_wait(first_full, 0, wctx))) break;
+      // Test only: the second tile is neither copied nor announced.
+      if (!(i == 1 && p.inject == kInjectSkipArrival)) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int row = 16 * wl + 4 * q + rsub;
-        const int64_t slotid = sanitize_slot(v[q], p.num_slots, p.status);
-        const uint8_t* ck = p.ckv + slotid * (kCkv * 2) + 16 * j;
-        const uint32_t dst = st_s + row * 128 + ((j ^ (row & 7)) << 4);
+        for (int q = 0; q < 4; ++q) {
+          const int row = 16 * wl + 4 * q + rsub;
+          const int64_t slotid = sanitize_slot(v[q], p.num_slots, p.status);
+          const uint8_t* ck = p.ckv + slotid * (kCkv * 2) + 16 * j;
+          const uint32_t dst = st_s + row * 128 + ((j ^ (row & 7)) << 4);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) cp_async16(dst + c * kChunkBytes, ck + 128 * c, policy);
-        cp_async16(dst + 8 * kChunkBytes, p.kpe + slotid * (kKpe * 2) + 16 * j, policy);
+          for (int c = 0; c < 8; ++c) cp_async16(dst + c * kChunkBytes, ck + 128 * c, policy);
+          cp_async16(dst + 8 * kChunkBytes, p.kpe + slotid * (kKpe * 2) + 16 * j, policy);
+        }
+        cp_async_wait_all();
+        fence_proxy_async_smem();
+        mbar_arrive(&kv_full[s]);
+        if (i == 0) mbar_arrive(first_full);
       }
-      cp_async_wait_all();
-      fence_proxy_async_smem();
-      mbar_arrive(&kv_full[s]);
 #pragma unroll
       for (int q = 0; q < 4; ++q) v[q] = nv[q];
     }
@@ -472,7 +593,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
           const unsigned long long now = global_timer_ns();
           if (t_idle == 0) {
             t_idle = now;
-          } else if (now - t_idle > kWaitLimitNs) {
+          } else if (now - t_idle > p.wait_limit_ns) {
             *abort_flag = 1;
             atomicOr(p.status, DSA_DEV_WAIT_TIMEOUT);
             break;
@@ -495,7 +616,9 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     const int srow = 16 * sp + (lane & 15);  // S^T row held by this thread (lane < 16)
     float m_run = -INFINITY, l_run = 0.f;
     int sg = -1, seg_first_tile = 0;
-    for (int i = 0; i < n; ++i) {
+    int owed_t = -1, owed_tk = 0;  // (thread 0) a ticket taken whose part is not settled yet
+    int i = 0;
+    for (; i < n; ++i) {
       const int64_t u = u0 + i;
       const int t = static_cast<int>(u / kTilesPerTok);
       const int tile = static_cast<int>(u % kTilesPerTok);
@@ -604,74 +727,117 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
       }
 
       if (seg_end) {
-        // ---- finalise the segment: wait for its last PV, drain O.
+        // ---- finalise the segment.  A split token's ticket is requested
+        // before the wait for the segment's last PV, so the atomic's round
+        // trip overlaps it.
+        const bool whole = (seg_first_tile == 0 && tile == kTilesPerTok - 1);
+        int ticket = 0;
+        if (!whole && e == 0) {
+          ticket = atomicAdd(p.tok_arrive + t, 1);
+          owed_t = t;
+          owed_tk = ticket;
+        }
         ok = mbar_wait(&p_empty[s], (i >> 1) & 1, wctx);
         tc_fence_after();
         if (g == 0) { ml_smem[2 * h] = m_run; ml_smem[2 * h + 1] = l_run; }
-        float o[4][16];
-        const uint32_t obuf = tmem_base + lane_base + kColO + 64u * (sg & 1);
-#pragma unroll
-        for (int mb = 0; mb < 4; ++mb) tmem_ld16(obuf + 16 * mb, o[mb]);
-        tmem_wait_ld();
-        tc_fence_before();
+        if (e == 0) *ticket_smem = ticket;
         if (!named_barrier_and(1, 128, ok)) break;
-        if (e == 0) mbar_arrive(&o_empty[sg & 1]);
-        const int col = 32 * sp + lane;
-        const bool whole = (seg_first_tile == 0 && tile == kTilesPerTok - 1);
+        const int col = 32 * sp + lane;  // == e: this thread's dims are 128 mb + col
+        const uint32_t obuf = tmem_base + lane_base + kColO + 64u * (sg & 1);
         if (whole) {
-          __nv_bfloat16* out = p.out + static_cast<int64_t>(t) * kHeads * kCkv;
+          if (e < kHeads) {  // 1 / l per head, for every thread
+            const float l = ml_smem[2 * e + 1];
+            alpha_smem[e] = l > 0.f ? 1.f / l : 0.f;
+          }
+          named_barrier_sync(1, 128);
+#pragma unroll 1
+          for (int mb = 0; mb < 4; ++mb) {
+            float o[16];
+            tmem_ld16(obuf + 16 * mb, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int hh = 0; hh < kHeads; ++hh) {
-            const float l = ml_smem[2 * hh + 1];
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-            for (int mb = 0; mb < 4; ++mb)
-              out[hh * kCkv + 128 * mb + col] = __float2bfloat16_rn(o[mb][hh] * inv);
+            for (int hh = 0; hh < kHeads; ++hh) o[hh] *= alpha_smem[hh];
+            store_out_column(p, t, 128 * mb + col, o);
           }
           if (e < kHeads) {
             const float l = ml_smem[2 * e + 1];
-            p.lse[static_cast<int64_t>(t) * kHeads + e] =
-                l > 0.f ? ml_smem[2 * e] + log2f(l) : -INFINITY;
+            p.lse[static_cast<int64_t>(t) * kHeads + e] = l > 0.f ? ml_smem[2 * e] + log2f(l) : -INFINITY;
           }
         } else {
-          const int64_t rec = static_cast<int64_t>(blockIdx.x) * p.kmax + (t - t_first);
-          __nv_bfloat16* po = p.part_o + rec * kHeads * kCkv;
-          // The part is stored normalised (O / l, |value| <= max |v|) in
-          // bf16: half the bytes for the merging CTA to read.
+          const int parts = parts_of(t, total, gridDim.x);
+          const int tk = *ticket_smem;
+          if (tk >= parts) {
+            // The counter was not zero on entry.  This kernel leaves every
+            // counter at zero, even after an abort, so the workspace was
+            // changed from outside (another workspace size, overlapping
+            // calls): report it.  The counter is left as it is, so every
+            // later call reports it too until the caller zero-fills the
+            // workspace; resetting it here could pair this call's
+            // publications with another call's tickets unnoticed.
+            if (e == 0) atomicOr(p.status, DSA_DEV_STALE_WORKSPACE);
+          } else if (tk < parts - 1 || parts > kInlineParts || i != n - 1) {
+            // Publish this part: O^T in fp32 as this thread holds it, then
+            // (m, l); the fence orders them before the publication count.
+            const int64_t rec = part_record(t, blockIdx.x, total, gridDim.x);
+            float* po = p.part_o + rec * kPartFloats + col * kHeads;
 #pragma unroll
-          for (int hh = 0; hh < kHeads; ++hh) {
-            const float l = ml_smem[2 * hh + 1];
-            const float inv = l > 0.f ? 1.f / l : 0.f;
+            for (int mb = 0; mb < 4; ++mb) {
+              float o[16];
+              tmem_ld16(obuf + 16 * mb, o);
+              tmem_wait_ld();
+              float4* dst = reinterpret_cast<float4*>(po + mb * 128 * kHeads);
 #pragma unroll
-            for (int mb = 0; mb < 4; ++mb) po[hh * kCkv + 128 * mb + col] = __float2bfloat16_rn(o[mb][hh] * inv);
+              for (int q = 0; q < 4; ++q) dst[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+            }
+            if (e < kHeads) {
+              p.part_ml[rec * 2 * kHeads + 2 * e] = ml_smem[2 * e];
+              p.part_ml[rec * 2 * kHeads + 2 * e + 1] = ml_smem[2 * e + 1];
+            }
+            __threadfence();
+            named_barrier_sync(1, 128);
+            if (e == 0) {
+              atomicAdd(p.tok_pub + t, 1);
+              // Deferred case: the last arriver merges every record once its
+              // own work is done (at most its first and last segments).
+              if (tk == parts - 1) merge_list[1 + merge_list[0]++] = t;
+            }
+          } else {
+            // The CTA's last segment: the K/V stage ring is idle (every PV
+            // has completed) and lands the other parts' records.
+            merge_inline(p, t, total, gridDim.x, obuf, ml_smem, reinterpret_cast<float*>(p_mem),
+                         stage_mem, e);
           }
-          if (e < kHeads) {
-            p.part_ml[rec * 2 * kHeads + 2 * e] = ml_smem[2 * e];
-            p.part_ml[rec * 2 * kHeads + 2 * e + 1] = ml_smem[2 * e + 1];
-          }
-          // Publish the partial, count it, and let the last CTA merge.
-          __threadfence();
-          named_barrier_sync(1, 128);
-          if (e == 0) {
-            const int parts = parts_of(t, total, gridDim.x);
-            const int prev = atomicAdd(p.tok_count + t, 1);
-            const int last = prev == parts - 1;
-            // The last part leaves the counter at zero for the next call; a
-            // count already at `parts` means the workspace held a stale one.
-            if (last) p.tok_count[t] = 0;
-            if (prev >= parts) atomicOr(p.status, DSA_DEV_STALE_WORKSPACE);
-            *rescale_flag = last ? 2 : 0;  // reuse the flag word as a broadcast
-          }
-          named_barrier_sync(1, 128);
-          const bool last = *rescale_flag == 2;
-          named_barrier_sync(1, 128);
-          if (e == 0) *rescale_flag = 0;
-          // Only a CTA's first and last segments can be partial, so it merges
-          // at most two tokens; it does so once all of its roles are done,
-          // with every thread of the CTA.
-          if (last && e == 0) merge_list[1 + merge_list[0]++] = t;
         }
-        named_barrier_sync(1, 128);  // ml_smem / sx are rewritten by the next segment
+        owed_t = -1;
+        // Every TMEM read of the O buffer has completed, and ml_smem, sx and
+        // the merge scratch are free for the next segment.
+        tc_fence_before();
+        named_barrier_sync(1, 128);
+        if (e == 0) mbar_arrive(&o_empty[sg & 1]);
+      }
+    }
+    if (i < n && e == 0) {
+      // The CTA aborted at tile i.  Its output is void (the status word says
+      // so), but the merge counters must still end at zero for later calls:
+      // settle every split token it had not finished, from tile i's on, as
+      // if its part had been published -- take the ticket (unless taken
+      // already), then publish, or, holding the last ticket, wait for the
+      // others and zero the counters.
+      const int t_end = static_cast<int>((u0 + n - 1) / kTilesPerTok);
+      for (int tt = static_cast<int>((u0 + i) / kTilesPerTok); tt <= t_end; ++tt) {
+        const int64_t a = static_cast<int64_t>(tt) * kTilesPerTok;
+        if (a >= u0 && a + kTilesPerTok <= u0 + n) continue;  // whole in this CTA: no counters
+        const int parts = parts_of(tt, total, gridDim.x);
+        const int tk = tt == owed_t ? owed_tk : atomicAdd(p.tok_arrive + tt, 1);
+        if (tk < parts - 1) {
+          atomicAdd(p.tok_pub + tt, 1);
+        } else if (tk == parts - 1) {
+          wait_counter_at_least(p.tok_pub + tt, parts - 1, p.status, 2 * p.wait_limit_ns);
+          p.tok_arrive[tt] = 0;
+          p.tok_pub[tt] = 0;
+        } else {
+          atomicOr(p.status, DSA_DEV_STALE_WORKSPACE);
+        }
       }
     }
   }
@@ -693,11 +859,10 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   }
   const int nmerge = merge_list[0];
   if (nmerge > 0) {
-    __threadfence();  // the other CTAs' partials, published before their counter bumps
     float* merge_sm = reinterpret_cast<float*>(p_mem);  // P and Sx, free now
     for (int k = 0; k < nmerge && k < 2; ++k) {
       if (k > 0) __syncthreads();  // the merge scratch is reused
-      merge_token(p, merge_list[1 + k], total, gridDim.x, merge_sm);
+      merge_deferred(p, merge_list[1 + k], total, gridDim.x, merge_sm);
     }
   }
 }
@@ -707,27 +872,40 @@ inline int grid_for(int num_tokens, int num_sms) {
   return static_cast<int>(units < num_sms ? units : num_sms);
 }
 
-inline int kmax_for(int num_tokens, int grid) {
-  const int64_t units = static_cast<int64_t>(num_tokens) * kTilesPerTok;
-  const int64_t per = (units + grid - 1) / grid;
-  return static_cast<int>((per + kTilesPerTok - 1) / kTilesPerTok + 1);
+// Workspace: header, [records][16][2] (m, l), [records][kPartFloats] O^T,
+// ..., [num_tokens] publication counters, [num_tokens] arrival counters at
+// the very end.
+inline size_t records_for(int num_tokens, int num_sms) {
+  return static_cast<size_t>(grid_for(num_tokens, num_sms)) * kRecsPerCta;
 }
 
 inline size_t workspace_for(int num_tokens, int num_sms) {
   if (num_tokens <= 0) return kWorkspaceHeader;
-  const int grid = grid_for(num_tokens, num_sms);
-  const size_t recs = static_cast<size_t>(grid) * kmax_for(num_tokens, grid);
-  return kWorkspaceHeader + recs * kHeads * (2 * sizeof(float) + kCkv * sizeof(__nv_bfloat16)) +
-         sizeof(int) * static_cast<size_t>(num_tokens);
+  return kWorkspaceHeader + records_for(num_tokens, num_sms) * (2 * kHeads + kPartFloats) * sizeof(float) +
+         2 * sizeof(int) * static_cast<size_t>(num_tokens);
 }
 
 std::once_flag g_attr_once[64];
 int g_attr_status[64];
 
+// One armed test fault (dsa_b200_test_inject), consumed by the next launch.
+std::atomic<unsigned long long> g_inject{0};  // kind << 56 | wait limit (ns), 0 = none
+
 }  // namespace attn
 }  // namespace dsa
 
 using namespace dsa;
+
+extern "C" int dsa_b200_test_inject(int kind, uint64_t wait_limit_ns) {
+  if (kind == DSA_TEST_NONE) {
+    attn::g_inject.store(0);
+    return DSA_OK;
+  }
+  if (kind != DSA_TEST_SKIP_ARRIVAL || wait_limit_ns == 0 || wait_limit_ns >= (1ull << 56))
+    return DSA_ERR_INVALID_ARGUMENT;
+  attn::g_inject.store((static_cast<unsigned long long>(kind) << 56) | wait_limit_ns);
+  return DSA_OK;
+}
 
 extern "C" size_t dsa_attention_workspace_bytes(int32_t num_tokens) {
   DeviceInfo info;
@@ -784,8 +962,7 @@ extern "C" int dsa_attention_run(const void* q_nope, const void* q_pe, const voi
     return st;
 
   const int grid = attn::grid_for(num_tokens, info.num_sms);
-  const int kmax = attn::kmax_for(num_tokens, grid);
-  const size_t recs = static_cast<size_t>(grid) * kmax;
+  const size_t recs = attn::records_for(num_tokens, info.num_sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   attn::Params prm;
   prm.indices = sparse_indices;
@@ -794,19 +971,28 @@ extern "C" int dsa_attention_run(const void* q_nope, const void* q_pe, const voi
   prm.out = static_cast<__nv_bfloat16*>(output);
   prm.lse = lse;
   prm.part_ml = reinterpret_cast<float*>(ws + kWorkspaceHeader);
-  prm.part_o = reinterpret_cast<__nv_bfloat16*>(prm.part_ml + recs * attn::kHeads * 2);
-  // The merge counters sit at the end of the buffer: every call leaves them
-  // at zero, and no call with another token count puts partial records
-  // there (records grow from the front, and workspace_for(T) >= records(T)
-  // + counters(T) with records(T) non-decreasing in T), so they need no
+  prm.part_o = prm.part_ml + recs * attn::kHeads * 2;
+  // The counters sit at the end of the buffer: every call leaves them at
+  // zero, and no call with another token count puts partial records there
+  // (records grow from the front, and workspace_for(T) >= records(T) +
+  // counters(T) with records(T) non-decreasing in T), so they need no
   // clearing as long as every call passes the same workspace_bytes.
-  prm.tok_count = reinterpret_cast<int*>(
-      ws + ((workspace_bytes - sizeof(int) * static_cast<size_t>(num_tokens)) & ~static_cast<size_t>(3)));
+  const size_t cnt_off = (workspace_bytes - 2 * sizeof(int) * static_cast<size_t>(num_tokens)) & ~static_cast<size_t>(3);
+  prm.tok_pub = reinterpret_cast<int*>(ws + cnt_off);
+  prm.tok_arrive = prm.tok_pub + num_tokens;
   prm.status = reinterpret_cast<unsigned int*>(ws);
   prm.num_slots = num_slots;
   prm.num_tokens = num_tokens;
-  prm.kmax = kmax;
   prm.scale_log2 = sm_scale * 1.4426950408889634f;
+  prm.wait_limit_ns = kWaitLimitNs;
+  prm.inject = attn::kInjectNone;
+  if (attn::g_inject.load(std::memory_order_relaxed) != 0) {
+    const unsigned long long armed = attn::g_inject.exchange(0);
+    if (armed != 0) {
+      prm.inject = static_cast<int>(armed >> 56);
+      prm.wait_limit_ns = armed & ((1ull << 56) - 1);
+    }
+  }
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (launch_programmatic(attn::attention_kernel, dim3(grid), dim3(attn::kThreads), attn::kSmemBytes,

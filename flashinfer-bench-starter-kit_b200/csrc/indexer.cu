@@ -15,8 +15,9 @@
 //                  resolved 32 tiles at a time, one group ahead, so no load
 //                  latency sits between two copy issues.  Nothing is dequantised in HBM
 //                  (the reference writes an fp32 copy of K, kernel.py:108-135).
-//      warps 10,11 MMA issuers (even / odd tiles; warp 10 also loads q[b],
-//                  64 heads x 128 B, when the request changes): tcgen05.mma kind::f8f6f4,
+//      warps 10-13 MMA issuers (warp 10+r takes the tiles n with n % 4 == r;
+//                  warp 10 also loads q[b], 64 heads x 128 B, when the
+//                  request changes): tcgen05.mma kind::f8f6f4,
 //                  M = 128 tokens, N = 64 heads, K = 128 (4 x K32), fp32
 //                  accumulator in TMEM, 4 accumulator stages; the K stage is
 //                  freed as soon as the MMAs complete.
@@ -38,8 +39,9 @@
 //    the score kernel overlaps through programmatic launch);
 //    one pass over the L scores then moves the winners of higher bins to the
 //    output and the boundary bin to a shared-memory candidate list, which
-//    later passes refine.  The 2048
-//    winners are bitonic-sorted and translated to global slot ids through
+//    later passes refine.  The 2048 winners are bucket-sorted on an 11-bit
+//    digit of their score (an in-warp bitonic + merge-path sort when the
+//    keys crowd into few buckets) and translated to global slot ids through
 //    the block table (kernel.py:156-169), then -1 padded (kernel.py:206).
 #include <algorithm>
 #include <mutex>
@@ -271,7 +273,7 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   const int u0 = static_cast<int>(total * blockIdx.x / gridDim.x);
   const int u1 = static_cast<int>(total * (blockIdx.x + 1) / gridDim.x);
   const int nt = u1 - u0;  // tiles of this CTA
-  const WaitCtx wctx{abort_flag, p.status};
+  const WaitCtx wctx{abort_flag, p.status, kWaitLimitNs};
 
   if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
     // ------------------------------------------------------ producer warps

@@ -319,7 +319,7 @@ prefill_score_kernel(const __grid_constant__ CUtensorMap kmap,
   const int u0 = static_cast<int>(total * blockIdx.x / gridDim.x);
   const int u1 = static_cast<int>(total * (blockIdx.x + 1) / gridDim.x);
   const int nt = u1 - u0;
-  const WaitCtx wctx{abort_flag, p.status};
+  const WaitCtx wctx{abort_flag, p.status, kWaitLimitNs};
 
   if (warp >= kProdWarp0 && warp < kProdWarp0 + kProdWarps) {
     // ------------------------------------------------------ producers

@@ -109,18 +109,19 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 struct WaitCtx {
   volatile int* abort_flag;
   unsigned int* status;
+  unsigned long long limit_ns;  // kWaitLimitNs, unless a test shortened it
 };
 
 // Waits for completion of the phase with the given parity.  Returns false
 // (without waiting further) if the CTA is aborting or the wait ran past
-// kWaitLimitNs, in which case it raises the abort flag and the status bit.
+// ctx.limit_ns, in which case it raises the abort flag and the status bit.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& ctx) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
     if (*ctx.abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > ctx.limit_ns) {
       *ctx.abort_flag = 1;
       atomicOr(ctx.status, DSA_DEV_WAIT_TIMEOUT);
       return false;
@@ -139,6 +140,31 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsig
     if (global_timer_ns() - t0 > 100000000ull) {  // 100 ms
       atomicOr(status, DSA_DEV_WAIT_TIMEOUT);
       return;
+    }
+  }
+}
+
+// Global-memory load with acquire semantics at GPU scope: later loads of
+// this thread see every write that the thread which released the value
+// (a fence before its store or atomic) made before it.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until *p >= target.  Gives up after limit_ns, raising
+// DSA_DEV_WAIT_TIMEOUT; returns whether the value was reached.
+__device__ __forceinline__ bool wait_counter_at_least(const int* p, int target, unsigned int* status,
+                                                      unsigned long long limit_ns) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (;;) {
+    __nanosleep(200);
+    if (ld_acquire_gpu(p) >= target) return true;
+    if (global_timer_ns() - t0 > limit_ns) {
+      atomicOr(status, DSA_DEV_WAIT_TIMEOUT);
+      return false;
     }
   }
 }

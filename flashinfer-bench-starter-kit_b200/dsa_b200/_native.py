@@ -43,7 +43,12 @@ SIGNATURES = {
     "dsa_indexer_prefill_run": (ctypes.c_int, [_P, _P, ctypes.c_int64, _P, _P, _P, _P, ctypes.c_int32,
                                                ctypes.c_int32, ctypes.c_int32, _P, _P, ctypes.c_size_t,
                                                _P]),
+    "dsa_b200_test_inject": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint64]),
 }
+
+# dsa_b200_test_inject kinds (failure-path tests only)
+TEST_NONE = 0
+TEST_SKIP_ARRIVAL = 1
 
 _lib = None
 _lock = threading.Lock()

@@ -55,3 +55,33 @@ def reduce_step_stats(ms_total: float, rank_bytes: float, rank_requests: float, 
     sm = stats.clone()
     dist.all_reduce(sm, op=dist.ReduceOp.SUM)
     return float(mx[0]), float(sm[1]), float(sm[2])
+
+
+def gather_outputs(tensors: list, world: int) -> list:
+    """All-gathers one decode shard's output tensors -- e.g. (topk_indices,
+    output, lse), each with the rank's requests as dimension 0 -- from every
+    rank, padded to the largest shard so one collective per tensor suffices.
+    Returns, per rank, the list of its tensors trimmed to its own request
+    count.  Every rank must call it (NCCL on GPUs, gloo on CPU); it is meant
+    for verification outside the timed region, never the hot path."""
+    import torch
+
+    if world <= 1:
+        return [list(tensors)]
+    import torch.distributed as dist
+
+    dev = tensors[0].device
+    n = torch.tensor([tensors[0].shape[0]], dtype=torch.int64, device=dev)
+    counts = [torch.zeros_like(n) for _ in range(world)]
+    dist.all_gather(counts, n)
+    counts = [int(c) for c in counts]
+    bmax = max(counts)
+    per_rank = [[] for _ in range(world)]
+    for t in tensors:
+        pad = torch.zeros((bmax,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        pad[: t.shape[0]] = t
+        parts = [torch.empty_like(pad) for _ in range(world)]
+        dist.all_gather(parts, pad)
+        for r in range(world):
+            per_rank[r].append(parts[r][: counts[r]])
+    return per_rank

@@ -113,13 +113,16 @@ DSA_API int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cache_f
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* Bytes of device workspace dsa_attention_run needs for num_tokens queries
- * on this device: a 256-byte header, the split-softmax partial records and
- * one merge counter per token, placed at the end of the workspace.  Zero-fill
- * a workspace once before its first use (status word and counters start at
- * zero; every completed call leaves the counters at zero again) and pass the
- * same workspace_bytes to every call on it.  After a call that raised
- * DSA_DEV_WAIT_TIMEOUT, zero-fill it again (a stale counter is reported as
- * DSA_DEV_STALE_WORKSPACE). */
+ * on this device: a 256-byte header, two split-softmax partial records per
+ * CTA (a token segment's O in fp32 and its per-head max and sum, 32.1 KiB
+ * each) and two merge counters per token, placed at the end of the
+ * workspace.  Zero-fill a workspace once before its first use (status word
+ * and counters start at zero) and pass the same workspace_bytes to every
+ * call on it.  Every call leaves the counters at zero again, including one
+ * that gave up on a bounded wait (DSA_DEV_WAIT_TIMEOUT).  A counter found
+ * non-zero on entry (the workspace was changed from outside, or two calls on
+ * it overlapped) is reported as DSA_DEV_STALE_WORKSPACE by this and every
+ * later call until the workspace is zero-filled again. */
 DSA_API size_t dsa_attention_workspace_bytes(int32_t num_tokens);
 
 /* Sparse MLA attention, one query token per row of sparse_indices.
@@ -237,6 +240,20 @@ DSA_API int dsa_index_cache_write(const void* k, const int64_t* slot_mapping, in
  * (errors there surface as Python exceptions, FAQ.md:238-240). */
 DSA_API int dsa_read_device_status(void* workspace, uint32_t* status_out, int clear,
                            void* stream);
+
+/* ---- test hook ---------------------------------------------------------
+ * Arms one fault for the next dsa_attention_run call made by any thread of
+ * this process (the call consumes it): `kind` DSA_TEST_SKIP_ARRIVAL makes,
+ * in every CTA, the producers of its second tile issue no copy and no
+ * arrival for it, and every bounded wait of that launch gives up after
+ * `wait_limit_ns` instead of 2 s.  The launch then ends with
+ * DSA_DEV_WAIT_TIMEOUT set and its output void; every wait stays bounded and
+ * the workspace's merge counters are left at zero, so the next call is
+ * exact.  kind DSA_TEST_NONE disarms.  For tests of the failure path only;
+ * no counterpart in the reference. */
+#define DSA_TEST_NONE         0
+#define DSA_TEST_SKIP_ARRIVAL 1
+DSA_API int dsa_b200_test_inject(int kind, uint64_t wait_limit_ns);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -125,9 +125,10 @@ def test_many_segments_per_cta(cuda_device, T):
 
 def test_merge_counters_are_left_zero_and_stale_ones_reported(cuda_device):
     # 64 tokens over the SM count: every token is split and merged.  Each
-    # call leaves its merge counters (at the end of the workspace) at zero;
-    # a counter planted non-zero is reported instead of silently skipping a
-    # merge.
+    # call leaves its merge counters (arrival tickets and publications, at
+    # the end of the workspace) at zero; an arrival counter planted non-zero
+    # is reported, by this call and the next, instead of silently pairing
+    # parts of different calls.
     T = 64
     a = workloads.make_attention_inputs(T, pool_pages=2048, seed=43, device=cuda_device)
     out, lse = run_gpu(a)
@@ -135,16 +136,49 @@ def test_merge_counters_are_left_zero_and_stale_ones_reported(cuda_device):
     dev = torch.device(cuda_device)
     buf = ws_mod.get(dev, "attention", 0, torch.cuda.current_stream(dev).cuda_stream)
     W = buf.numel()
-    off = (W - 4 * T) & ~3
-    assert int(buf[off:off + 4 * T].view(torch.int32).abs().sum()) == 0
-    buf[off:off + 4].view(torch.int32).fill_(1000)
+    off = (W - 8 * T) & ~3
+    assert int(buf[off:off + 8 * T].view(torch.int32).abs().sum()) == 0
+    arrive0 = off + 4 * T
+    buf[arrive0:arrive0 + 4].view(torch.int32).fill_(1000)
     try:
-        with pytest.raises(DsaError, match="merge counter"):
-            run_gpu(a)
+        for _ in range(2):
+            with pytest.raises(DsaError, match="merge counter"):
+                run_gpu(a)
     finally:
         buf.zero_()
     out, lse = run_gpu(a)
     check(a, out, lse, tokens=[0, 31, 63])
+
+
+@pytest.mark.parametrize("T", [64, 5])
+def test_wait_timeout_is_reported_and_the_next_call_is_exact(cuda_device, T):
+    # The failure path, made to happen without faulting anything: a test hook
+    # makes every CTA's producers skip their second tile (no copy is issued,
+    # no barrier arrival made) and shortens every bounded wait to 1 ms.  The
+    # MMA issuers' wait for that tile runs out, the CTA aborts, drains and
+    # frees its tensor memory, and settles the merge counters of the tokens
+    # it still owed.  The call must return with DSA_DEV_WAIT_TIMEOUT set, and
+    # the next call on the same workspace must be exact.  T = 5 gives tokens
+    # of many parts (merged from records at the end of a CTA); T = 64 tokens
+    # of 3-4 parts (merged by the last one as its segment ends).
+    from dsa_b200 import _native
+    a = workloads.make_attention_inputs(T, pool_pages=2048, seed=600 + T, device=cuda_device)
+    good_out, good_lse = run_gpu(a)
+    check(a, good_out, good_lse, tokens=[0, T // 2, T - 1])
+    dev = torch.device(cuda_device)
+    buf = ws_mod.get(dev, "attention", 0, torch.cuda.current_stream(dev).cuda_stream)
+    lib = _native.lib()
+    assert lib.dsa_b200_test_inject(_native.TEST_SKIP_ARRIVAL, 1_000_000) == 0
+    try:
+        with pytest.raises(DsaError, match="timed out"):
+            run_gpu(a)
+    finally:
+        lib.dsa_b200_test_inject(_native.TEST_NONE, 0)
+    W = buf.numel()
+    off = (W - 8 * T) & ~3
+    assert int(buf[off:off + 8 * T].view(torch.int32).abs().sum()) == 0, "merge counters left set"
+    out, lse = run_gpu(a)
+    assert torch.equal(out, good_out) and torch.equal(lse, good_lse)
 
 
 def test_large_logits_rescale(cuda_device):

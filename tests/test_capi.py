@@ -89,6 +89,14 @@ def test_attention_misaligned():
                                  1 << 30, NULL) == 2
 
 
+def test_test_hook_validation():
+    lib = _native.lib()
+    assert lib.dsa_b200_test_inject(7, 1000) == 1           # unknown kind
+    assert lib.dsa_b200_test_inject(_native.TEST_SKIP_ARRIVAL, 0) == 1
+    assert lib.dsa_b200_test_inject(_native.TEST_SKIP_ARRIVAL, 1000) == 0
+    assert lib.dsa_b200_test_inject(_native.TEST_NONE, 0) == 0  # disarm again
+
+
 def test_read_status_rejects_null():
     lib = _native.lib()
     out = ctypes.c_uint32(0)

@@ -13,7 +13,9 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from dsa_b200 import sharding, workloads
+from oracle import attention as oatt
 from oracle import indexer as oix
+from oracle import parity
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 8])
@@ -53,6 +55,12 @@ def _problem():
     return workloads.make_indexer_inputs(LENS, pool_pages=260, seed=77, device=torch.device("cpu"))
 
 
+def _decode_problem(rank):
+    # shards of different sizes: rank r holds 2 + r requests
+    lens = [300 + 500 * i for i in range(2 + rank)]
+    return workloads.make_decode_inputs(lens, seed=50 + rank, device=torch.device("cpu"))
+
+
 def _rank_main(rank, world, port, out_dir):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -71,9 +79,26 @@ def _rank_main(rank, world, port, out_dir):
         flag = torch.tensor([1], dtype=torch.int32)
         flags = [torch.zeros_like(flag) for _ in range(world)]
         dist.all_gather(flags, flag)
+        # bench.py's verify(): every rank's (indices, output, lse) gathered to
+        # rank 0 (shards of different sizes), plus the sampled rows' oracle
+        # bundles; rank 0 checks the gathered outputs against the oracle.
+        # Here the "outputs" are the oracle's own, computed per rank.
+        dec = _decode_problem(rank)
+        d_topk, _ = oix.indexer_reference(dec.indexer.q_index_fp8, dec.indexer.k_index_cache_fp8,
+                                          dec.indexer.weights, dec.indexer.seq_lens,
+                                          dec.indexer.block_table)
+        d_out, d_lse = oatt.attention_reference(dec.q_nope, dec.q_pe, dec.ckv_cache, dec.kpe_cache,
+                                                d_topk, dec.sm_scale)
+        outs = sharding.gather_outputs([d_topk, d_out, d_lse], world)
+        B = d_topk.shape[0]
+        bundles = [None] * world
+        dist.all_gather_object(bundles, parity.pack_rows(dec, d_topk, [0, B - 1], rank))
         if rank == 0:
+            rep = parity.check_bundles([b for bs in bundles for b in bs], outs)
             torch.save({"stats": (ms, nbytes, nreq), "gathered": gathered,
-                        "flags": [int(f.item()) for f in flags]}, os.path.join(out_dir, "r0.pt"))
+                        "flags": [int(f.item()) for f in flags],
+                        "out_rows": [o[0].shape[0] for o in outs], "parity": rep},
+                       os.path.join(out_dir, "r0.pt"))
     finally:
         dist.destroy_process_group()
 
@@ -91,6 +116,10 @@ def test_two_gloo_ranks_match_a_single_process(tmp_path):
     r = torch.load(tmp_path / "r0.pt")
     assert r["stats"] == (2.0, 300.0, float(len(LENS)))
     assert r["flags"] == [1, 1]
+    assert r["out_rows"] == [2, 3]
+    rep = r["parity"]
+    assert rep["ok"], rep["problems"]
+    assert rep["rows"] == 4 and rep["exact_rows"] == 4 and rep["tokens"] == 4
     ix = _problem()
     full, _ = oix.indexer_reference(ix.q_index_fp8, ix.k_index_cache_fp8, ix.weights,
                                     ix.seq_lens, ix.block_table)
