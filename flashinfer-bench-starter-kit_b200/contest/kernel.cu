@@ -19,21 +19,48 @@
 
 namespace {
 
-std::mutex g_mu;
-std::map<std::tuple<int, int, cudaStream_t>, torch::Tensor> g_ws;  // (device, op, stream)
+// Streams whose workspace is kept per (device, operator); a harness that
+// makes a fresh stream per run would otherwise keep every old buffer.
+constexpr int kMaxStreamsPerOp = 8;
 
+struct Entry {
+  torch::Tensor buf;
+  uint64_t last_use = 0;
+};
+
+std::mutex g_mu;
+std::map<std::tuple<int, int, cudaStream_t>, Entry> g_ws;  // (device, op, stream)
+uint64_t g_calls = 0;
+
+// Calls on different streams may run concurrently, so each stream has its
+// own buffer.  Beyond kMaxStreamsPerOp streams of a (device, operator) the
+// least recently used buffer is dropped: the caching allocator hands its
+// memory out again only to later work on the stream it was allocated on
+// (the one it served), which is ordered after every kernel that used it.
 torch::Tensor workspace(const torch::Device& dev, int op, size_t bytes, cudaStream_t stream) {
   std::lock_guard<std::mutex> lock(g_mu);
-  auto key = std::make_tuple(static_cast<int>(dev.index()), op, stream);
+  const int device = static_cast<int>(dev.index());
+  auto key = std::make_tuple(device, op, stream);
   auto it = g_ws.find(key);
-  if (it == g_ws.end() || static_cast<size_t>(it->second.numel()) < bytes) {
-    // Zero-filled once; the kernels clear what must start at zero themselves.
-    auto t = torch::zeros({static_cast<int64_t>(bytes)},
-                          torch::TensorOptions().dtype(torch::kUInt8).device(dev));
-    g_ws[key] = t;
-    return t;
+  if (it == g_ws.end()) {
+    int n = 0;
+    auto lru = g_ws.end();
+    for (auto e = g_ws.begin(); e != g_ws.end(); ++e) {
+      if (std::get<0>(e->first) != device || std::get<1>(e->first) != op) continue;
+      ++n;
+      if (lru == g_ws.end() || e->second.last_use < lru->second.last_use) lru = e;
+    }
+    if (n >= kMaxStreamsPerOp && lru != g_ws.end()) g_ws.erase(lru);
+    it = g_ws.emplace(key, Entry{}).first;
   }
-  return it->second;
+  Entry& e = it->second;
+  e.last_use = ++g_calls;
+  if (!e.buf.defined() || static_cast<size_t>(e.buf.numel()) < bytes) {
+    // Zero-filled once; the kernels clear what must start at zero themselves.
+    e.buf = torch::zeros({static_cast<int64_t>(bytes)},
+                         torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+  }
+  return e.buf;
 }
 
 void check(int st, const char* what) {

@@ -33,22 +33,52 @@ using tvm::ffi::TensorView;
 struct Buffer {
   void* ptr = nullptr;
   size_t bytes = 0;
+  uint64_t last_use = 0;  // call counter of the entry's latest use
 };
+
+// Streams whose workspace is kept per (device, operator); a harness that
+// makes a fresh stream per run would otherwise keep every old buffer.
+constexpr int kMaxStreamsPerOp = 8;
 
 std::mutex g_mu;
 std::map<std::tuple<int, int, cudaStream_t>, Buffer> g_ws;  // (device, op, stream)
+uint64_t g_calls = 0;
 
 // The buffer is passed with its full size on every call: the attention
-// kernels place their merge counters at its end.
+// kernels place their merge counters at its end.  Calls on different
+// streams may run concurrently, so each stream has its own buffer; beyond
+// kMaxStreamsPerOp streams of a (device, operator) the least recently used
+// buffer is freed (cudaFree waits for the device, so no kernel still reads
+// it; skipped while the stream is being captured, where freeing is illegal).
 Buffer workspace(int device, int op, size_t bytes, cudaStream_t stream) {
   std::lock_guard<std::mutex> lock(g_mu);
-  Buffer& b = g_ws[std::make_tuple(device, op, stream)];
+  const auto key = std::make_tuple(device, op, stream);
+  auto it = g_ws.find(key);
+  if (it == g_ws.end()) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(stream, &cap);
+    int n = 0;
+    auto lru = g_ws.end();
+    for (auto e = g_ws.begin(); e != g_ws.end(); ++e) {
+      if (std::get<0>(e->first) != device || std::get<1>(e->first) != op) continue;
+      ++n;
+      if (lru == g_ws.end() || e->second.last_use < lru->second.last_use) lru = e;
+    }
+    if (n >= kMaxStreamsPerOp && cap == cudaStreamCaptureStatusNone && lru != g_ws.end()) {
+      cudaFree(lru->second.ptr);
+      g_ws.erase(lru);
+    }
+    it = g_ws.emplace(key, Buffer{}).first;
+  }
+  Buffer& b = it->second;
+  b.last_use = ++g_calls;
   if (b.bytes >= bytes) return b;
   // cudaFree waits for the device, so kernels still reading the old buffer
   // finish first; the new one is zero-filled once (the kernels clear what
   // must start at zero on every call themselves).
   if (b.ptr != nullptr) cudaFree(b.ptr);
-  b = Buffer{};
+  b.ptr = nullptr;
+  b.bytes = 0;
   void* p = nullptr;
   if (cudaMalloc(&p, bytes) != cudaSuccess || cudaMemset(p, 0, bytes) != cudaSuccess) {
     if (p != nullptr) cudaFree(p);

@@ -37,8 +37,9 @@
 //   its partial (O in fp32, m, l) and then bumps the token's publication
 //   counter; the last one waits until the others have published -- they
 //   have all arrived already, so the wait is short and cannot depend on a
-//   CTA that is not running -- and merges them with its own accumulator
-//   straight from TMEM, without storing its own part:
+//   CTA that is not running -- and, once its own tiles are done, merges
+//   them with all of its threads, its own part read straight from TMEM
+//   when the token is its last segment:
 //   lse = log2 L + M with L = sum_i l_i 2^(m_i - M),
 //   out = sum_i O_i 2^(m_i - M) / L.
 //   The counters sit at the end of the workspace; the merging CTA resets its
@@ -77,18 +78,33 @@ constexpr int kTmemCols = 256;
 constexpr uint32_t kColO = 0;    // O^T buffers at [0,64) and [64,128): 4 blocks x 16 heads
 constexpr uint32_t kColS = 128;  // S^T buffers at [128,192) and [192,256): 4 partial sums x 16 heads
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: factor 256
+constexpr unsigned long long kSecondTileDelayNs = 1000;
 constexpr int kMaxTokens = (1 << 30) / (kTopK / kRows) / kHeads;
 // Most parts a token can have (its 32 tiles meet at most 33 CTA slices); the
 // merge scratch holds the parts' per-head weights ([kMaxParts][16] floats)
 // and record indices.
 constexpr int kMaxParts = 48;
-// A partial record: the part's O^T, [4 column blocks][128 dims][16 heads]
-// fp32 -- the order in which the 128 softmax threads hold it (thread e: dims
-// 128 mb + e, all heads), so each thread moves 64 contiguous bytes per block.
+// A partial record: the part's O^T in fp32 as float4s of 4 heads,
+// [4 column blocks mb][4 head quads q][128 dims][4 heads]: thread e of the
+// softmax warps (dims 128 mb + e, all heads) writes float4 (mb, q, e), and
+// consecutive threads touch consecutive 16 bytes, both when a part is
+// published and when it is merged.
 constexpr int kPartFloats = 4 * 128 * kHeads;  // 8192 floats = 32 KiB
+__device__ __forceinline__ int part_index(int mb, int q, int dim_in_block) {
+  return (mb * 4 + q) * 128 + dim_in_block;  // float4 index inside a record
+}
 // Only a CTA's first and last token segments can be partial: two records
 // per CTA, slot 0 for its first segment and slot 1 for its last.
 constexpr int kRecsPerCta = 2;
+// Parts whose records one merging thread loads at once (16 floats each)
+// when they do not fit the landing area.
+constexpr int kMergeBatch = 2;
+// Parts that land in the idle K/V stage ring (32 KiB each) during a merge.
+constexpr int kLandParts = 4;
+static_assert(kLandParts * kPartFloats * 4 <= 2 * kStageBytes, "landing area");
+// Merge scratch in shared memory: per part and head the max m and sum l
+// (then the weight), the parts' record indices and a flag.
+constexpr int kMergeScratchBytes = 2 * (kMaxParts * kHeads * 4) + kMaxParts * 8 + 16;
 
 // bf16 x bf16 -> f32.  Logits: A = K rows (K-major), B = Q (K-major), M64 N16.
 constexpr uint32_t kIdescS = idesc_make(1, 1, false, false, 64, 16);
@@ -102,10 +118,9 @@ constexpr int kOffSx = kOffP + 2 * kPBytes;          // 188416
 constexpr int kOffBar = kOffSx + kHeads * kRows * 4; // 192512
 constexpr int kOffMisc = kOffBar + 256;
 constexpr int kSmemBytes = 1024 + kOffMisc + 256;
-static_assert((18 + kMmaWarps + 1) * 8 <= 256, "barrier area");
-static_assert(kOffSx == kOffP + 2 * kPBytes &&
-                  2 * kPBytes + kHeads * kRows * 4 >= (kMaxParts + 1) * kHeads * 4 + kMaxParts * 8,
-              "merge scratch: the P and Sx buffers, contiguous");
+static_assert((18 + kMmaWarps + 2) * 8 <= 256, "barrier area");
+static_assert(kOffSx == kOffP + 2 * kPBytes && 2 * kPBytes + kHeads * kRows * 4 >= kMergeScratchBytes,
+              "the P and Sx buffers, contiguous, hold the merge scratch");
 
 // Test-only fault injection (dsa_b200_test_inject): the producer group of
 // each CTA's second tile issues no copy and no arrival for it, so the MMA
@@ -165,41 +180,6 @@ __device__ __forceinline__ int64_t part_record(int t, int c, int64_t total, int 
   return static_cast<int64_t>(c) * kRecsPerCta + (t == tf ? 0 : 1);
 }
 
-// A token of up to this many parts whose last part is its CTA's last
-// segment is merged by that CTA's softmax threads as soon as the segment
-// ends, its own part read straight from TMEM.  Otherwise (many parts, at
-// small token counts where CTAs hold few tiles, or a last part that is the
-// CTA's first segment) every part is published as a record and the last
-// arriver merges them with all of its threads once its own tiles are done.
-constexpr int kInlineParts = 4;
-
-// Per-head merge weights of token t's parts, by threads e < 16 (head e):
-// wts[i][e] = 2^(m_i - M) / L for parts i = 0 .. nparts-1 in CTA order,
-// lse = M + log2 L.  Part i's (m, l) come from its record, except for the
-// caller's own part (recs[i] < 0), whose (m, l) per head are own_ml.  The
-// sums run in part order whichever CTA merges, so a call's result does not
-// depend on which CTA arrived last.
-__device__ __forceinline__ void merge_weights(const Params& p, int t, int nparts, const int64_t* recs,
-                                              const float* own_ml, float* wts, int e) {
-  float M = -INFINITY;
-  for (int i = 0; i < nparts; ++i) {
-    const float m = recs[i] < 0 ? own_ml[2 * e] : __ldcg(p.part_ml + recs[i] * 2 * kHeads + 2 * e);
-    wts[i * kHeads + e] = m;
-    M = fmaxf(M, m);
-  }
-  float L = 0.f;
-  for (int i = 0; i < nparts; ++i) {
-    const float m = wts[i * kHeads + e];
-    const float w = m == -INFINITY ? 0.f : exp2f(m - M);
-    const float l = recs[i] < 0 ? own_ml[2 * e + 1] : __ldcg(p.part_ml + recs[i] * 2 * kHeads + 2 * e + 1);
-    L += l * w;
-    wts[i * kHeads + e] = w;
-  }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  for (int i = 0; i < nparts; ++i) wts[i * kHeads + e] *= inv;
-  p.lse[static_cast<int64_t>(t) * kHeads + e] = L > 0.f ? M + log2f(L) : -INFINITY;
-}
-
 // Writes 16 heads of output dim `dim` of token t (bf16).
 __device__ __forceinline__ void store_out_column(const Params& p, int t, int dim, const float (&acc)[16]) {
   __nv_bfloat16* out = p.out + static_cast<int64_t>(t) * kHeads * kCkv + dim;
@@ -207,146 +187,169 @@ __device__ __forceinline__ void store_out_column(const Params& p, int t, int dim
   for (int hh = 0; hh < kHeads; ++hh) out[hh * kCkv] = __float2bfloat16_rn(acc[hh]);
 }
 
-// Every wait on a publication counter is bounded by twice the pipeline
-// limit: a CTA that holds a ticket publishes (or settles, after an abort) at
-// most one pipeline wait later, so a waiter never gives up on a part that
-// is still coming.
-
-// Inline merge by the 128 softmax threads of the CTA holding token t's last
-// part (nparts <= kInlineParts), at the end of the CTA's last segment: its
-// own O^T is in TMEM at `obuf` (this thread's lanes), its (m, l) per head in
-// own_ml; the other parts are records.  Each thread copies its 64 bytes per
-// column block of every other record into `landing` (the idle K/V stage
-// ring) with cp.async, all in flight together and overlapping the (m, l)
-// loads of the weights, then combines them with its TMEM accumulator.
-// scratch: (kMaxParts + 1) * 16 floats + kMaxParts int64.
-__device__ __forceinline__ void merge_inline(const Params& p, int t, int64_t total, int grid, uint32_t obuf,
-                                             const float* own_ml, float* scratch, uint8_t* landing, int e) {
+// Merges split token t once this CTA's own work is done, with all kThreads
+// threads.  Parts are the covering CTAs c_lo..c_hi in order; every part's
+// O^T and (m, l) come from its record, except this CTA's own part when
+// `own_obuf` names the TMEM columns of its last segment's O^T accumulator
+// (own_ml: its (m, l) per head), in which case it never left the SM.  Waits
+// (bounded) until the other parts have published.  The weights
+// w_i = 2^(m_i - M) / L per head and the weighted sums run in part order,
+// so the result does not depend on which CTA merges:
+//   lse = M + log2 L, L = sum_i l_i 2^(m_i - M), out = sum_i w_i O_i.
+// Up to kLandParts parts' records are brought into `landing` (the idle K/V
+// stage ring) by one bulk copy each, completing on `land_bar` (phase
+// `land_parity`), while the weights' (m, l) loads are in flight; more parts
+// (small token counts) are read from L2 kMergeBatch parts at a time.
+// Thread -> warp w reads TMEM sub-partition w & 3 (dims 32 (w & 3) + lane of
+// each 128-dim block) and block mb = w >> 2: one output dim, 16 heads.
+// Returns whether the landing barrier was used (its phase then advanced).
+__device__ bool merge_at_end(const Params& p, int t, int64_t total, int grid, int own_obuf,
+                             const float* own_ml, uint32_t tmem_base, uint8_t* scratch, uint8_t* landing,
+                             uint64_t* land_bar, uint32_t land_parity) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int c_lo, c_hi;
   covering_ctas(t, total, grid, c_lo, c_hi);
   const int nparts = c_hi - c_lo + 1;
-  float* wts = scratch;
-  int64_t* recs = reinterpret_cast<int64_t*>(scratch + (kMaxParts + 1) * kHeads);
-  if (e < nparts) {
-    const int c = c_lo + e;
-    recs[e] = c == static_cast<int>(blockIdx.x) ? -1 : part_record(t, c, total, grid);
+  float* wm = reinterpret_cast<float*>(scratch);          // [kMaxParts][16] m, then weights
+  float* wl = wm + kMaxParts * kHeads;                     // [kMaxParts][16] l
+  int64_t* recs = reinterpret_cast<int64_t*>(wl + kMaxParts * kHeads);
+  int* flag = reinterpret_cast<int*>(recs + kMaxParts);
+  if (nparts > kMaxParts) {  // cannot happen for grids of <= 2^20 CTAs; never read past scratch
+    if (tid == 0) atomicOr(p.status, DSA_DEV_BAD_INDEX);
+    return false;
   }
-  bool ok = true;
-  if (e == 0) ok = wait_counter_at_least(p.tok_pub + t, nparts - 1, p.status, 2 * p.wait_limit_ns);
-  if (named_barrier_and(1, 128, ok)) {
-    const uint32_t land = smem_u32(landing);
-    const uint64_t policy = make_policy_evict_first();
-    for (int i = 0; i < nparts; ++i) {
-      if (recs[i] < 0) continue;
-      const float* src = p.part_o + recs[i] * kPartFloats + e * kHeads;
-#pragma unroll
-      for (int mb = 0; mb < 4; ++mb)
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          cp_async16(land + (((i * 4 + mb) * 128 + e) * 4 + q) * 16, src + mb * 128 * kHeads + 4 * q, policy);
+  const bool own_tmem = own_obuf >= 0;
+  if (tid < nparts) {
+    const int c = c_lo + tid;
+    recs[tid] = (own_tmem && c == static_cast<int>(blockIdx.x)) ? -1 : part_record(t, c, total, grid);
+  }
+  __syncthreads();  // recs
+  const bool land = nparts <= kLandParts;
+  if (tid == 0) {
+    const bool ok = wait_counter_at_least(p.tok_pub + t, own_tmem ? nparts - 1 : nparts, p.status,
+                                          2 * p.wait_limit_ns);
+    *flag = ok ? 1 : 0;
+    if (land) {
+      // The acquire above made the records visible to this thread; the proxy
+      // fence extends that to its bulk copies.
+      fence_proxy_async_global();
+      uint32_t bytes = 0;
+      for (int i = 0; i < nparts; ++i) bytes += (ok && recs[i] >= 0) ? kPartFloats * 4 : 0;
+      mbar_arrive_expect_tx(land_bar, bytes);  // completes the phase at once when nothing is copied
+      for (int i = 0; i < nparts; ++i)
+        if (ok && recs[i] >= 0)
+          bulk_load(landing + i * kPartFloats * 4, p.part_o + recs[i] * kPartFloats, kPartFloats * 4, land_bar);
     }
-    if (e < kHeads) merge_weights(p, t, nparts, recs, own_ml, wts, e);
-    cp_async_wait_all();  // this thread's own copies; it alone reads them
-    named_barrier_sync(1, 128);
-#pragma unroll 1
-    for (int mb = 0; mb < 4; ++mb) {
-      float own[16], acc[16];
-      tmem_ld16(obuf + 16 * mb, own);
-      tmem_wait_ld();
+  }
+  __syncthreads();  // flag
+  const int sp = warp & 3, mb = warp >> 2;
+  const int de = 32 * sp + lane;  // dim inside the 128-dim block
+  if (*flag && tid < kHeads) {
+    // (m, l) of every part, eight parts' loads in flight at a time.
+    const int e = tid;
+    float M = -INFINITY;
+    for (int i0 = 0; i0 < nparts; i0 += 8) {
+      float mv[8], lv[8];
 #pragma unroll
-      for (int hh = 0; hh < kHeads; ++hh) acc[hh] = 0.f;
-      for (int i = 0; i < nparts; ++i) {  // part order: the same sums whoever merges
-        const float* wv = wts + i * kHeads;
+      for (int k = 0; k < 8; ++k) {
+        const int i = i0 + k;
+        mv[k] = -INFINITY;
+        lv[k] = 0.f;
+        if (i < nparts) {
+          if (recs[i] < 0) {
+            mv[k] = own_ml[2 * e];
+            lv[k] = own_ml[2 * e + 1];
+          } else {
+            mv[k] = __ldcg(p.part_ml + recs[i] * 2 * kHeads + 2 * e);
+            lv[k] = __ldcg(p.part_ml + recs[i] * 2 * kHeads + 2 * e + 1);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (i0 + k < nparts) {
+          wm[(i0 + k) * kHeads + e] = mv[k];
+          wl[(i0 + k) * kHeads + e] = lv[k];
+          M = fmaxf(M, mv[k]);
+        }
+      }
+    }
+    float L = 0.f;
+    for (int i = 0; i < nparts; ++i) {
+      const float m = wm[i * kHeads + e];
+      const float w = m == -INFINITY ? 0.f : exp2f(m - M);
+      L += wl[i * kHeads + e] * w;
+      wm[i * kHeads + e] = w;
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    for (int i = 0; i < nparts; ++i) wm[i * kHeads + e] *= inv;
+    p.lse[static_cast<int64_t>(t) * kHeads + e] = L > 0.f ? M + log2f(L) : -INFINITY;
+  }
+  // Every thread waits for the landing (bounded; a copy cannot hang, this
+  // only guards the bookkeeping) before the weights barrier.
+  if (land) mbar_drain(land_bar, land_parity, p.status);
+  __syncthreads();  // weights
+  if (*flag) {
+    float own[16];
+    if (own_tmem) {
+      tc_fence_after();
+      tmem_ld16(tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + own_obuf + 16 * mb, own);
+      tmem_wait_ld();
+    }
+    float acc[16];
+#pragma unroll
+    for (int hh = 0; hh < kHeads; ++hh) acc[hh] = 0.f;
+    auto add = [&](const float4 (&v)[4], int i) {
+      const float4* wv = reinterpret_cast<const float4*>(wm + i * kHeads);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 w = wv[q];
+        acc[4 * q] = fmaf(v[q].x, w.x, acc[4 * q]);
+        acc[4 * q + 1] = fmaf(v[q].y, w.y, acc[4 * q + 1]);
+        acc[4 * q + 2] = fmaf(v[q].z, w.z, acc[4 * q + 2]);
+        acc[4 * q + 3] = fmaf(v[q].w, w.w, acc[4 * q + 3]);
+      }
+    };
+    if (land) {
+      for (int i = 0; i < nparts; ++i) {
+        float4 v[4];
         if (recs[i] < 0) {
 #pragma unroll
-          for (int hh = 0; hh < kHeads; ++hh) acc[hh] = fmaf(own[hh], wv[hh], acc[hh]);
+          for (int q = 0; q < 4; ++q) v[q] = make_float4(own[4 * q], own[4 * q + 1], own[4 * q + 2], own[4 * q + 3]);
         } else {
-          const float4* f = reinterpret_cast<const float4*>(landing + (((i * 4 + mb) * 128 + e) * 4) * 16);
+          const float4* f = reinterpret_cast<const float4*>(landing + i * kPartFloats * 4);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 x = f[q];
-            acc[4 * q] = fmaf(x.x, wv[4 * q], acc[4 * q]);
-            acc[4 * q + 1] = fmaf(x.y, wv[4 * q + 1], acc[4 * q + 1]);
-            acc[4 * q + 2] = fmaf(x.z, wv[4 * q + 2], acc[4 * q + 2]);
-            acc[4 * q + 3] = fmaf(x.w, wv[4 * q + 3], acc[4 * q + 3]);
+          for (int q = 0; q < 4; ++q) v[q] = f[part_index(mb, q, de)];
+        }
+        add(v, i);
+      }
+    } else {
+      for (int i0 = 0; i0 < nparts; i0 += kMergeBatch) {
+        float4 v[kMergeBatch][4];
+#pragma unroll
+        for (int k = 0; k < kMergeBatch; ++k) {
+          const int i = i0 + k;
+          if (i < nparts && recs[i] >= 0) {
+            const float4* src = reinterpret_cast<const float4*>(p.part_o + recs[i] * kPartFloats);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[k][q] = __ldcg(src + part_index(mb, q, de));
+          } else if (i < nparts) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[k][q] = make_float4(own[4 * q], own[4 * q + 1], own[4 * q + 2], own[4 * q + 3]);
           }
         }
+#pragma unroll
+        for (int k = 0; k < kMergeBatch; ++k)
+          if (i0 + k < nparts) add(v[k], i0 + k);
       }
-      store_out_column(p, t, 128 * mb + e, acc);
     }
+    store_out_column(p, t, 128 * mb + de, acc);
   }
-  if (e == 0) {  // the token's counters are zero again for the next call
+  if (tid == 0) {  // the token's counters are zero again for the next call
     p.tok_arrive[t] = 0;
     p.tok_pub[t] = 0;
   }
-}
-
-// Deferred merge of token t (nparts > kInlineParts) from every part's record,
-// by all kThreads threads of the last arriver once its own work is done.
-// Thread -> float4 j = tid + 512 q (q < 4) of each 2048-float4 record, i.e.
-// dims 128 mb + e and heads 4 g .. 4 g + 3 with j = (mb * 128 + e) * 4 + g;
-// four parts' loads are in flight per round.  sm: as merge_inline's scratch.
-__device__ __forceinline__ void merge_deferred(const Params& p, int t, int64_t total, int grid, float* sm) {
-  const int tid = threadIdx.x;
-  int c_lo, c_hi;
-  covering_ctas(t, total, grid, c_lo, c_hi);
-  const int nparts = c_hi - c_lo + 1;
-  float* wts = sm;
-  int64_t* recs = reinterpret_cast<int64_t*>(sm + (kMaxParts + 1) * kHeads);
-  if (nparts > kMaxParts) {  // cannot happen for grids of <= 2^20 CTAs; never read past sm
-    if (tid == 0) atomicOr(p.status, DSA_DEV_BAD_INDEX);
-    return;
-  }
-  if (tid < nparts) recs[tid] = part_record(t, c_lo + tid, total, grid);
-  int* flag = reinterpret_cast<int*>(recs + kMaxParts);
-  if (tid == 0) *flag = wait_counter_at_least(p.tok_pub + t, nparts, p.status, 2 * p.wait_limit_ns) ? 1 : 0;
-  __syncthreads();
-  if (*flag) {
-    if (tid < kHeads) merge_weights(p, t, nparts, recs, nullptr, wts, tid);
-    __syncthreads();
-    float acc[4][4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) acc[q][k] = 0.f;
-    for (int i0 = 0; i0 < nparts; i0 += 4) {
-      float4 v[4][4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (i0 + k < nparts) {
-          const float4* src = reinterpret_cast<const float4*>(p.part_o + recs[i0 + k] * kPartFloats);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) v[k][q] = __ldcg(src + tid + 512 * q);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (i0 + k < nparts) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float* wv = wts + (i0 + k) * kHeads + 4 * ((tid + 512 * q) & 3);
-            acc[q][0] = fmaf(v[k][q].x, wv[0], acc[q][0]);
-            acc[q][1] = fmaf(v[k][q].y, wv[1], acc[q][1]);
-            acc[q][2] = fmaf(v[k][q].z, wv[2], acc[q][2]);
-            acc[q][3] = fmaf(v[k][q].w, wv[3], acc[q][3]);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int j = tid + 512 * q;
-      const int g = j & 3, de = j >> 2;  // de = mb * 128 + e
-      const int dim = de;                 // dims 128 mb + e, in order
-      __nv_bfloat16* out = p.out + static_cast<int64_t>(t) * kHeads * kCkv + dim;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) out[(4 * g + k) * kCkv] = __float2bfloat16_rn(acc[q][k]);
-    }
-  }
-  if (tid == 0) {
-    p.tok_arrive[t] = 0;
-    p.tok_pub[t] = 0;
-  }
+  return land;
 }
 
 __device__ __forceinline__ int sanitize_slot(int v, int64_t num_slots, unsigned int* status) {
@@ -382,11 +385,13 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   uint64_t* drain = bars + 18;  // one per MMA warp
   // Single-use: completes when the CTA's first tile has landed (group 0).
   uint64_t* first_full = bars + 18 + kMmaWarps;
+  // Merges: the bulk copies of other parts' records into the stage ring.
+  uint64_t* land_bar = bars + 19 + kMmaWarps;
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   int* abort_flag = reinterpret_cast<int*>(smem + kOffMisc + 4);
-  int* rescale_flag = reinterpret_cast<int*>(smem + kOffMisc + 8);
-  int* merge_list = reinterpret_cast<int*>(smem + kOffMisc + 12);  // count, then <= 2 tokens
-  int* ticket_smem = reinterpret_cast<int*>(smem + kOffMisc + 24);
+  int* ticket_smem = reinterpret_cast<int*>(smem + kOffMisc + 8);
+  // count, then <= 2 (token, TMEM column of the own part's O^T or -1) pairs
+  int* merge_list = reinterpret_cast<int*>(smem + kOffMisc + 12);
   int* q_last = reinterpret_cast<int*>(smem + kOffMisc + 32);      // last segment loaded per Q slot
   float* alpha_smem = reinterpret_cast<float*>(smem + kOffMisc + 64);   // 16
   float* ml_smem = reinterpret_cast<float*>(smem + kOffMisc + 128);     // 16 x (m, l)
@@ -400,13 +405,13 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
       mbar_init(&kv_full[s], 32 * kProdWarps / 2); mbar_init(&kv_empty[s], kMmaWarps);
       mbar_init(&q_full[s], 1);  mbar_init(&q_empty[s], kMmaWarps);
       mbar_init(&s_full[s], kMmaWarps);  mbar_init(&s_empty[s], 128);
-      mbar_init(&p_full[s], 1);  mbar_init(&p_empty[s], kMmaWarps);
+      mbar_init(&p_full[s], 128);  mbar_init(&p_empty[s], kMmaWarps);
       mbar_init(&o_empty[s], 1);
     }
     for (int w = 0; w < kMmaWarps; ++w) mbar_init(&drain[w], 1);
     mbar_init(first_full, 32 * kProdWarps / 2);
+    mbar_init(land_bar, 1);
     *abort_flag = 0;
-    *rescale_flag = 0;
     merge_list[0] = 0;
     q_last[0] = q_last[1] = -1;
     fence_mbar_init();
@@ -491,10 +496,11 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
       }
       const int s = g;
       if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ((i >> 1) & 1) ^ 1, wctx))) break;
-      // The second tile's rows are requested only once the first tile's have
-      // landed: with every SM starting at once, the first tile then arrives
-      // in about half the time and the MMA / softmax chain starts earlier.
-      if (i == 1 && !__all_sync(0xffffffffu, mbar_wait(first_full, 0, wctx))) break;
+      // With every SM starting at once, the first tile lands sooner when
+      // the second one's rows are requested a little later: give the first
+      // tile a head start of up to kSecondTileDelayNs (an ordering hint;
+      // running out is not an error).
+      if (i == 1) mbar_wait_at_most(first_full, 0, kSecondTileDelayNs);
       // Test only: the second tile is neither copied nor announced.
       if (!(i == 1 && p.inject == kInjectSkipArrival)) {
 #pragma unroll
@@ -605,18 +611,30 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     }
   } else {
     // ------------------------------------------------------ softmax warps
-    // Every bounded wait is followed, before any branch, by a named barrier
-    // that ANDs the threads' results, so the 128 threads always meet the same
-    // barriers and leave the loop together if a wait gave up.
+    // Thread (warp sp, lane) reads S^T row 16 sp + (lane & 15) (the M = 64
+    // accumulator occupies TMEM lanes 0-15 of each sub-partition) straight
+    // from TMEM -- no shared-memory transpose and, in the common case, one
+    // barrier per tile; lane L < 16 weights heads 0-7 of its row and lane
+    // L + 16 heads 8-15 of the same row.  The running max m_run[h] is the same in
+    // every thread; it moves only when some row of the tile exceeds it by more
+    // than kRescaleThreshold (always at a segment's first tile), which the
+    // threads learn from one OR-reduction barrier; only then is the tile's
+    // per-head max reduced across the rows.  The softmax denominators are
+    // kept per row (l_row[h]) and summed over the rows once per segment.
+    // Every bounded wait's result joins the tile's reduction barrier, so the
+    // 128 threads always meet the same barriers and leave the loop together if
+    // a wait gave up.
     const int sp = warp & 3;
     const int e = tid - 32 * kSoftWarp0; // 0..127
-    const int h = e >> 3;                // head owned in the reduction phase
-    const int g = e & 7;                 // 8-row group of that head
+    const bool row_lane = lane < 16;
     const uint32_t lane_base = static_cast<uint32_t>(sp * 32) << 16;
     const int srow = 16 * sp + (lane & 15);  // S^T row held by this thread (lane < 16)
-    float m_run = -INFINITY, l_run = 0.f;
+    float* red = sx;  // reduction scratch: tile maxima [2][4 warps][16 heads], row sums [4][16]
+    const int h0 = (lane >> 4) * 8;           // first of this lane's 8 heads
+    float m_run[kHeads], l_row[8];
     int sg = -1, seg_first_tile = 0;
     int owed_t = -1, owed_tk = 0;  // (thread 0) a ticket taken whose part is not settled yet
+    bool ok = true;
     int i = 0;
     for (; i < n; ++i) {
       const int64_t u = u0 + i;
@@ -624,107 +642,104 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
       const int tile = static_cast<int>(u % kTilesPerTok);
       const bool seg_start = (i == 0 || tile == 0);
       const bool seg_end = (i == n - 1 || tile == kTilesPerTok - 1);
-      if (seg_start) { ++sg; m_run = -INFINITY; l_run = 0.f; seg_first_tile = tile; }
+      if (seg_start) {
+        ++sg;
+        seg_first_tile = tile;
+#pragma unroll
+        for (int hh = 0; hh < kHeads; ++hh) m_run[hh] = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) l_row[k] = 0.f;
+      }
       const int s = i & 1;
       const int idx = __ldg(p.indices + static_cast<int64_t>(t) * kTopK + tile * kRows + srow);
-      const bool valid = idx >= 0 && idx < p.num_slots;
+      const bool valid = row_lane && idx >= 0 && idx < p.num_slots;
 
-      bool ok = mbar_wait(&s_full[s], (i >> 1) & 1, wctx);
+      ok = mbar_wait(&s_full[s], (i >> 1) & 1, wctx) && ok;
       tc_fence_after();
-      float sv[16];
+      float x[kHeads];
       {
         float lo[32], hi[32];
         tmem_ld32(tmem_base + lane_base + kColS + 64u * s, lo);
         tmem_ld32(tmem_base + lane_base + kColS + 64u * s + 32, hi);
         tmem_wait_ld();
 #pragma unroll
-        for (int hh = 0; hh < kHeads; ++hh) sv[hh] = (lo[hh] + lo[16 + hh]) + (hi[hh] + hi[16 + hh]);
+        for (int hh = 0; hh < kHeads; ++hh)
+          x[hh] = valid ? ((lo[hh] + lo[16 + hh]) + (hi[hh] + hi[16 + hh])) * p.scale_log2 : -INFINITY;
       }
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
-      if (lane < 16) {
+      bool need = false;
 #pragma unroll
-        for (int hh = 0; hh < kHeads; ++hh)
-          sx[hh * kRows + srow] = valid ? sv[hh] * p.scale_log2 : -INFINITY;
-      }
-      if (!named_barrier_and(1, 128, ok)) break;
-
-      float x[8];
-      {
-        const float4 a = *reinterpret_cast<const float4*>(sx + h * kRows + 8 * g);
-        const float4 b = *reinterpret_cast<const float4*>(sx + h * kRows + 8 * g + 4);
-        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-      }
-      float mt = x[0];
+      for (int hh = 0; hh < kHeads; ++hh) need |= x[hh] > m_run[hh] + kRescaleThreshold;
+      if (named_barrier_or(1, 128, need || !ok)) {
+        // ---- slow path: a wait gave up, or the running max moves.
+        if (!named_barrier_and(1, 128, ok)) break;
+        // Per-head tile max: a warp max (redux on order-preserving keys),
+        // then the four warps' maxima through shared memory.  The scratch
+        // half alternates with the tile, so the next slow path cannot
+        // overwrite it before every thread has read it.
+        float* rmax = red + 64 * (i & 1);
 #pragma unroll
-      for (int k = 1; k < 8; ++k) mt = fmaxf(mt, x[k]);
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
-      float m_new = m_run, alpha = 1.f;
-      bool need_rescale = false;
-      if (seg_start) {
-        m_new = mt;
-      } else if (mt > m_run + kRescaleThreshold) {
-        m_new = mt;
-        alpha = exp2f(m_run - m_new);  // 0 when m_run == -inf
-        need_rescale = true;
-      }
-      float pr[8], sum = 0.f;
+        for (int hh = 0; hh < kHeads; ++hh) {
+          const uint32_t k = __reduce_max_sync(0xffffffffu, float_order_key(x[hh]));
+          if (lane == 0) rmax[sp * kHeads + hh] = float_from_order_key(k);
+        }
+        named_barrier_sync(1, 128);
+        bool any_alpha = false;
+        float alpha[kHeads];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        pr[k] = (m_new == -INFINITY) ? 0.f : exp2f(x[k] - m_new);
-        sum += pr[k];
-      }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-      l_run = l_run * alpha + sum;
-      m_run = m_new;
-      if (g == 0) {
-        alpha_smem[h] = alpha;
-        if (need_rescale) *rescale_flag = 1;
+        for (int hh = 0; hh < kHeads; ++hh) {
+          const float mt = fmaxf(fmaxf(rmax[hh], rmax[kHeads + hh]), fmaxf(rmax[2 * kHeads + hh], rmax[3 * kHeads + hh]));
+          alpha[hh] = 1.f;
+          if (mt > m_run[hh] + kRescaleThreshold) {
+            alpha[hh] = exp2f(m_run[hh] - mt);  // 0 when m_run == -inf
+            m_run[hh] = mt;
+            any_alpha = true;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) l_row[k] *= lane < 16 ? alpha[k] : alpha[8 + k];
+        if (any_alpha && !seg_start) {
+          // O must hold PV(i-1) before it is rescaled (same segment: i >= 1).
+          ok = mbar_wait(&p_empty[(i - 1) & 1], ((i - 1) >> 1) & 1, wctx) && ok;
+          tc_fence_after();
+          const uint32_t obuf = tmem_base + lane_base + kColO + 64u * (sg & 1);
+#pragma unroll
+          for (int mb = 0; mb < 4; ++mb) {
+            float o[16];
+            tmem_ld16(obuf + 16 * mb, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int hh = 0; hh < kHeads; ++hh) o[hh] *= alpha[hh];
+            tmem_st16(obuf + 16 * mb, o);
+          }
+          tmem_wait_st();
+        }
       }
       // P buffer s was last read by the PV of tile i-2.
-      if (i >= 2) ok = mbar_wait(&p_empty[s], ((i - 2) >> 1) & 1, wctx);
+      if (i >= 2) ok = mbar_wait(&p_empty[s], ((i - 2) >> 1) & 1, wctx) && ok;
       {
-        __nv_bfloat162 q0 = __floats2bfloat162_rn(pr[0], pr[1]);
-        __nv_bfloat162 q1 = __floats2bfloat162_rn(pr[2], pr[3]);
-        __nv_bfloat162 q2 = __floats2bfloat162_rn(pr[4], pr[5]);
-        __nv_bfloat162 q3 = __floats2bfloat162_rn(pr[6], pr[7]);
-        uint4 pk;
-        pk.x = *reinterpret_cast<uint32_t*>(&q0);
-        pk.y = *reinterpret_cast<uint32_t*>(&q1);
-        pk.z = *reinterpret_cast<uint32_t*>(&q2);
-        pk.w = *reinterpret_cast<uint32_t*>(&q3);
-        uint8_t* dst = p_mem + s * kPBytes + (h >> 3) * 1024 + (h & 7) * 128 + ((g ^ (h & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = pk;
-      }
-      if (!named_barrier_and(1, 128, ok)) break;
-      if (*rescale_flag) {
-        // O must hold PV(i-1) before it is rescaled (same segment: i >= 1).
-        ok = mbar_wait(&p_empty[(i - 1) & 1], ((i - 1) >> 1) & 1, wctx);
-        tc_fence_after();
-        const uint32_t obuf = tmem_base + lane_base + kColO + 64u * (sg & 1);
+        // Lane L + 16 takes heads 8-15 of lane L's row.
+        float xs[8], ms[8];
 #pragma unroll
-        for (int mb = 0; mb < 4; ++mb) {
-          float o[16];
-          tmem_ld16(obuf + 16 * mb, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int hh = 0; hh < kHeads; ++hh) o[hh] *= alpha_smem[hh];
-          tmem_st16(obuf + 16 * mb, o);
+        for (int k = 0; k < 8; ++k) {
+          const float hi = __shfl_sync(0xffffffffu, x[8 + k], lane & 15);
+          xs[k] = lane < 16 ? x[k] : hi;
+          ms[k] = lane < 16 ? m_run[k] : m_run[8 + k];
         }
-        tmem_wait_st();
+        // P^T, K-major 128-byte swizzled: head h's 64 rows are 128 bytes,
+        // 16-byte piece g holds rows 8g .. 8g + 7.
+        uint8_t* pb = p_mem + s * kPBytes + (h0 >> 3) * 1024 + (srow & 7) * 2;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float pr = ms[k] == -INFINITY ? 0.f : ex2_approx(xs[k] - ms[k]);
+          l_row[k] += pr;
+          *reinterpret_cast<__nv_bfloat16*>(pb + k * 128 + (((srow >> 3) ^ k) << 4)) = __float2bfloat16_rn(pr);
+        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      if (!named_barrier_and(1, 128, ok)) break;
-      if (e == 0) {
-        *rescale_flag = 0;
-        mbar_arrive(&p_full[s]);
-      }
+      mbar_arrive(&p_full[s]);
 
       if (seg_end) {
         // ---- finalise the segment.  A split token's ticket is requested
@@ -737,11 +752,28 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
           owed_t = t;
           owed_tk = ticket;
         }
-        ok = mbar_wait(&p_empty[s], (i >> 1) & 1, wctx);
+        ok = mbar_wait(&p_empty[s], (i >> 1) & 1, wctx) && ok;
         tc_fence_after();
-        if (g == 0) { ml_smem[2 * h] = m_run; ml_smem[2 * h + 1] = l_run; }
-        if (e == 0) *ticket_smem = ticket;
+        // Per-head denominators: the row sums added over the 64 rows (lanes
+        // 0-15 hold heads 0-7, lanes 16-31 heads 8-15).
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float v = l_row[k];
+          v += __shfl_xor_sync(0xffffffffu, v, 8);
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          if ((lane & 15) == 0) red[128 + sp * kHeads + h0 + k] = v;
+        }
+        if (e == 0) {
+          *ticket_smem = ticket;
+#pragma unroll
+          for (int hh = 0; hh < kHeads; ++hh) ml_smem[2 * hh] = m_run[hh];
+        }
         if (!named_barrier_and(1, 128, ok)) break;
+        if (e < kHeads)
+          ml_smem[2 * e + 1] = (red[128 + e] + red[128 + kHeads + e]) + (red[128 + 2 * kHeads + e] + red[128 + 3 * kHeads + e]);
+        named_barrier_sync(1, 128);
         const int col = 32 * sp + lane;  // == e: this thread's dims are 128 mb + col
         const uint32_t obuf = tmem_base + lane_base + kColO + 64u * (sg & 1);
         if (whole) {
@@ -775,19 +807,19 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             // workspace; resetting it here could pair this call's
             // publications with another call's tickets unnoticed.
             if (e == 0) atomicOr(p.status, DSA_DEV_STALE_WORKSPACE);
-          } else if (tk < parts - 1 || parts > kInlineParts || i != n - 1) {
+          } else if (tk < parts - 1 || i != n - 1) {
             // Publish this part: O^T in fp32 as this thread holds it, then
             // (m, l); the fence orders them before the publication count.
             const int64_t rec = part_record(t, blockIdx.x, total, gridDim.x);
-            float* po = p.part_o + rec * kPartFloats + col * kHeads;
+            float4* po = reinterpret_cast<float4*>(p.part_o + rec * kPartFloats);
 #pragma unroll
             for (int mb = 0; mb < 4; ++mb) {
               float o[16];
               tmem_ld16(obuf + 16 * mb, o);
               tmem_wait_ld();
-              float4* dst = reinterpret_cast<float4*>(po + mb * 128 * kHeads);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) dst[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+              for (int q = 0; q < 4; ++q)
+                po[part_index(mb, q, col)] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
             }
             if (e < kHeads) {
               p.part_ml[rec * 2 * kHeads + 2 * e] = ml_smem[2 * e];
@@ -797,15 +829,20 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             named_barrier_sync(1, 128);
             if (e == 0) {
               atomicAdd(p.tok_pub + t, 1);
-              // Deferred case: the last arriver merges every record once its
-              // own work is done (at most its first and last segments).
-              if (tk == parts - 1) merge_list[1 + merge_list[0]++] = t;
+              // The last arriver at its first segment (its O buffer is
+              // reused later) merges from records once its work is done.
+              if (tk == parts - 1) {
+                merge_list[1 + 2 * merge_list[0]] = t;
+                merge_list[2 + 2 * merge_list[0]] = -1;
+                ++merge_list[0];
+              }
             }
-          } else {
-            // The CTA's last segment: the K/V stage ring is idle (every PV
-            // has completed) and lands the other parts' records.
-            merge_inline(p, t, total, gridDim.x, obuf, ml_smem, reinterpret_cast<float*>(p_mem),
-                         stage_mem, e);
+          } else if (e == 0) {
+            // The last arriver at its last segment: its part stays in TMEM
+            // and the merge runs once every role is done, with all threads.
+            merge_list[1 + 2 * merge_list[0]] = t;
+            merge_list[2 + 2 * merge_list[0]] = static_cast<int>(kColO + 64u * (sg & 1));
+            ++merge_list[0];
           }
         }
         owed_t = -1;
@@ -844,10 +881,6 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp0) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
-  }
   if (warp == kProdWarp0 && lane == 0) {
     // A Q load still in flight (only after an abort) must land before exit.
     // Only the last load of each slot can be: loading segment s + 2 waits
@@ -857,13 +890,20 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     for (int k = 0; k < 2; ++k)
       if (q_last[k] >= 0) mbar_drain(&q_full[k], (q_last[k] >> 1) & 1, p.status);
   }
+  // Split tokens this CTA merges (at most its first and last segments).
   const int nmerge = merge_list[0];
-  if (nmerge > 0) {
-    float* merge_sm = reinterpret_cast<float*>(p_mem);  // P and Sx, free now
-    for (int k = 0; k < nmerge && k < 2; ++k) {
-      if (k > 0) __syncthreads();  // the merge scratch is reused
-      merge_deferred(p, merge_list[1 + k], total, gridDim.x, merge_sm);
-    }
+  uint32_t land_parity = 0;
+  for (int k = 0; k < nmerge && k < 2; ++k) {
+    if (k > 0) __syncthreads();  // the merge scratch (P and Sx buffers, free now) and landing are reused
+    if (merge_at_end(p, merge_list[1 + 2 * k], total, gridDim.x, merge_list[2 + 2 * k], ml_smem, tmem_base,
+                     p_mem, stage_mem, land_bar, land_parity))
+      land_parity ^= 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp0) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 

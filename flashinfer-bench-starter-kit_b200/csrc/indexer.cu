@@ -150,12 +150,6 @@ __device__ __forceinline__ void locate(const int* tile_off, int batch, int64_t u
   j = static_cast<int>(u - tile_off[b]);
 }
 
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
-
 // What the producer needs to know about one tile; each lane of the producer
 // warp resolves one tile of a 32-tile group so the block-table loads of a
 // whole group are in flight together (and one group ahead).

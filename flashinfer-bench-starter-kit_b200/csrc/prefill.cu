@@ -221,12 +221,6 @@ __global__ void __launch_bounds__(kPlanThreads, 1) prefill_plan_kernel(const Pla
   }
 }
 
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
-
 // Group g with tile_off[g] <= u < tile_off[g + 1].
 __device__ __forceinline__ int locate_group(const int* tile_off, int ngroups, int64_t u) {
   int lo = 0, hi = ngroups - 1;

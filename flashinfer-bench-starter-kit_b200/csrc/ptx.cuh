@@ -129,6 +129,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
+// Waits at most `ns` for the phase with the given parity; returns whether it
+// completed (giving up is not an error: for ordering hints only).
+__device__ __forceinline__ bool mbar_wait_at_most(uint64_t* bar, uint32_t parity, unsigned long long ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (global_timer_ns() - t0 < ns)
+    if (mbar_try_wait_sleep(bar, parity, 200)) return true;
+  return false;
+}
+
 // Short bounded wait used while tearing down: lets an asynchronous copy or
 // MMA that may still be in flight complete before the CTA exits.  In a run
 // without an abort the phase has completed already.  Giving up (100 ms)
@@ -188,6 +198,20 @@ __device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t nthreads
   return r != 0;
 }
 
+// Named barrier that ORs a flag over the participating threads.
+__device__ __forceinline__ bool named_barrier_or(uint32_t id, uint32_t nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -213,6 +237,21 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* m
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)),
         "r"(x), "r"(y), "l"(policy)
       : "memory");
+}
+
+// Untiled bulk copy of `bytes` (a multiple of 16, both addresses 16-byte
+// aligned) from global into shared memory; completes tx bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+// Orders this thread's earlier global-memory accesses (e.g. an acquire load
+// that made other SMs' writes visible) before its later async-proxy (bulk
+// copy) reads of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // Row gather: 4 rows (r0..r3) x one box width starting at column x.  The map's
@@ -450,6 +489,25 @@ __device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, f
 __device__ __forceinline__ float relu_nan(float x) {
   float y;
   asm("max.NaN.f32 %0, %1, 0f00000000;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Order-preserving uint32 image of a float (larger float, larger key) and
+// its inverse: integer max reductions (redux.sync) then give float maxima.
+__device__ __forceinline__ uint32_t float_order_key(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float float_from_order_key(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// 2^x by the MUFU unit (PTX ex2.approx.ftz.f32: about 2 ulp, results below
+// the normal range flushed to zero).  For softmax weights 2^(x - m) with
+// x <= m + 8, where a flushed 2^-126 does not change any sum.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
