@@ -16,9 +16,12 @@ entry points, the C ABI and the kernels.  Three variants:
            "torch": contest/kernel.cu::dsa_indexer / ::dsa_attention.
   tvm-ffi  language "cuda", binding "tvm-ffi" (the harness's default
            binding): contest/kernel_tvm.cu::dsa_indexer / ::dsa_attention.
-  python   language "python": contest/kernel.py::run_indexer /
-           ::run_attention, which compile the packed CUDA sources for sm_100a
-           themselves through tvm_ffi.cpp.load.  The harness's CUDA builders
+  python   language "python": kernel.py::run, the entry point name the
+           reference's config.toml files use (dsa_indexer/config.toml:8,
+           dsa_attention/config.toml:7).  Each operator's packed kernel.py is
+           contest/kernel.py plus a `run` with that operator's arguments,
+           calling run_indexer / run_attention, which compile the packed CUDA
+           sources for sm_100a themselves through tvm_ffi.cpp.load.  The harness's CUDA builders
            set no SM target and take no flags (FAQ.md:144-154), so this is the
            variant that builds the sm_100a kernels under a stock harness.
 """
@@ -48,7 +51,22 @@ VARIANTS = {
     "cuda": ("cuda", "torch", "kernel.cu", [HERE / "kernel.cu"], None),
     "tvm-ffi": ("cuda", "tvm-ffi", "kernel_tvm.cu", [HERE / "kernel_tvm.cu"], None),
     "python": ("python", None, "kernel.py", [HERE / "kernel.py", HERE / "kernel_tvm.cu"],
-               {"dsa_indexer": "run_indexer", "dsa_attention": "run_attention"}),
+               {"dsa_indexer": "run", "dsa_attention": "run"}),
+}
+# The python variant's per-operator entry point, appended to its kernel.py.
+PY_RUN = {
+    "dsa_indexer": '''
+
+def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices):
+    """The operator's entry point, kernel.py::run (dsa_indexer/config.toml:8)."""
+    run_indexer(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices)
+''',
+    "dsa_attention": '''
+
+def run(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse):
+    """The operator's entry point, kernel.py::run (dsa_attention/config.toml:7)."""
+    run_attention(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse)
+''',
 }
 
 
@@ -71,7 +89,9 @@ def solution(op: str, variant: str = "cuda") -> dict:
         "definition": sol["definition"],
         "author": sol["author"],
         "spec": spec,
-        "sources": [{"path": p.name, "content": p.read_text()} for p in front + LIBRARY],
+        "sources": [{"path": p.name,
+                     "content": p.read_text() + (PY_RUN[op] if variant == "python" and p.name == "kernel.py" else "")}
+                    for p in front + LIBRARY],
     }
 
 

@@ -194,7 +194,8 @@ def test_python_solution_matches_the_library_and_captures(cuda_device, tmp_path,
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):  # first calls on the capture stream size its workspaces
-        sol.run_indexer(ix.q_index_fp8, ix.k_index_cache_fp8, ix.weights, ix.seq_lens, ix.block_table, got)
+        # kernel.py::run, the packed indexer's entry point (as the reference names it)
+        sol.run(ix.q_index_fp8, ix.k_index_cache_fp8, ix.weights, ix.seq_lens, ix.block_table, got)
         sol.run_attention(dec.q_nope, dec.q_pe, dec.ckv_cache, dec.kpe_cache, got, dec.sm_scale, o2, l2)
     torch.cuda.synchronize()
     assert torch.equal(got, want)
