@@ -103,8 +103,16 @@ constexpr int kMergeBatch = 2;
 constexpr int kLandParts = 4;
 static_assert(kLandParts * kPartFloats * 4 <= 2 * kStageBytes, "landing area");
 // Merge scratch in shared memory: per part and head the max m and sum l
-// (then the weight), the parts' record indices and a flag.
-constexpr int kMergeScratchBytes = 2 * (kMaxParts * kHeads * 4) + kMaxParts * 8 + 16;
+// (then the weight), and a flag.
+constexpr int kMergeScratchBytes = 2 * (kMaxParts * kHeads * 4) + 16;
+// Parts of the CTA's first (slot 0) and last (slot 1) token, the only ones
+// it can merge: per slot the first covering CTA, the part count and each
+// part's record index, computed while the first tile is in flight.
+struct MergeParts {
+  int c_lo[2];
+  int nparts[2];
+  int64_t rec[2][kMaxParts];
+};
 
 // bf16 x bf16 -> f32.  Logits: A = K rows (K-major), B = Q (K-major), M64 N16.
 constexpr uint32_t kIdescS = idesc_make(1, 1, false, false, 64, 16);
@@ -117,7 +125,8 @@ constexpr int kOffP = kOffQ + 2 * kQBytes;           // 184320
 constexpr int kOffSx = kOffP + 2 * kPBytes;          // 188416
 constexpr int kOffBar = kOffSx + kHeads * kRows * 4; // 192512
 constexpr int kOffMisc = kOffBar + 256;
-constexpr int kSmemBytes = 1024 + kOffMisc + 256;
+constexpr int kOffParts = kOffMisc + 256;
+constexpr int kSmemBytes = 1024 + kOffParts + static_cast<int>(sizeof(MergeParts));
 static_assert((18 + kMmaWarps + 2) * 8 <= 256, "barrier area");
 static_assert(kOffSx == kOffP + 2 * kPBytes && 2 * kPBytes + kHeads * kRows * 4 >= kMergeScratchBytes,
               "the P and Sx buffers, contiguous, hold the merge scratch");
@@ -197,56 +206,54 @@ __device__ __forceinline__ void store_out_column(const Params& p, int t, int dim
 // so the result does not depend on which CTA merges:
 //   lse = M + log2 L, L = sum_i l_i 2^(m_i - M), out = sum_i w_i O_i.
 // Up to kLandParts parts' records are brought into `landing` (the idle K/V
-// stage ring) by one bulk copy each, completing on `land_bar` (phase
-// `land_parity`), while the weights' (m, l) loads are in flight; more parts
-// (small token counts) are read from L2 kMergeBatch parts at a time.
+// stage ring) by one bulk copy each (thread 0), completing on `land_bar`
+// (phase `land_parity`), while warps 2-3 load the weights' (m, l); more
+// parts (small token counts) are read from L2 kMergeBatch parts at a time.
+// The parts' record indices come precomputed in `parts` (slot `slot`).
 // Thread -> warp w reads TMEM sub-partition w & 3 (dims 32 (w & 3) + lane of
 // each 128-dim block) and block mb = w >> 2: one output dim, 16 heads.
 // Returns whether the landing barrier was used (its phase then advanced).
-__device__ bool merge_at_end(const Params& p, int t, int64_t total, int grid, int own_obuf,
+__device__ bool merge_at_end(const Params& p, int t, const MergeParts& parts, int slot, int own_obuf,
                              const float* own_ml, uint32_t tmem_base, uint8_t* scratch, uint8_t* landing,
                              uint64_t* land_bar, uint32_t land_parity) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int c_lo, c_hi;
-  covering_ctas(t, total, grid, c_lo, c_hi);
-  const int nparts = c_hi - c_lo + 1;
+  const int nparts = parts.nparts[slot];
   float* wm = reinterpret_cast<float*>(scratch);          // [kMaxParts][16] m, then weights
   float* wl = wm + kMaxParts * kHeads;                     // [kMaxParts][16] l
-  int64_t* recs = reinterpret_cast<int64_t*>(wl + kMaxParts * kHeads);
-  int* flag = reinterpret_cast<int*>(recs + kMaxParts);
+  int* flag = reinterpret_cast<int*>(wl + kMaxParts * kHeads);
   if (nparts > kMaxParts) {  // cannot happen for grids of <= 2^20 CTAs; never read past scratch
     if (tid == 0) atomicOr(p.status, DSA_DEV_BAD_INDEX);
     return false;
   }
   const bool own_tmem = own_obuf >= 0;
-  if (tid < nparts) {
-    const int c = c_lo + tid;
-    recs[tid] = (own_tmem && c == static_cast<int>(blockIdx.x)) ? -1 : part_record(t, c, total, grid);
-  }
-  __syncthreads();  // recs
+  // Part i's record index, or -1 for this CTA's own part kept in TMEM.
+  const int own_i = own_tmem ? static_cast<int>(blockIdx.x) - parts.c_lo[slot] : -1;
+  auto rec = [&](int i) -> int64_t { return i == own_i ? -1 : parts.rec[slot][i]; };
   const bool land = nparts <= kLandParts;
   if (tid == 0) {
     const bool ok = wait_counter_at_least(p.tok_pub + t, own_tmem ? nparts - 1 : nparts, p.status,
                                           2 * p.wait_limit_ns);
     *flag = ok ? 1 : 0;
-    if (land) {
-      // The acquire above made the records visible to this thread; the proxy
-      // fence extends that to its bulk copies.
-      fence_proxy_async_global();
-      uint32_t bytes = 0;
-      for (int i = 0; i < nparts; ++i) bytes += (ok && recs[i] >= 0) ? kPartFloats * 4 : 0;
-      mbar_arrive_expect_tx(land_bar, bytes);  // completes the phase at once when nothing is copied
-      for (int i = 0; i < nparts; ++i)
-        if (ok && recs[i] >= 0)
-          bulk_load(landing + i * kPartFloats * 4, p.part_o + recs[i] * kPartFloats, kPartFloats * 4, land_bar);
-    }
+    if (land && !ok) mbar_arrive_expect_tx(land_bar, 0);  // completes the phase at once
   }
   __syncthreads();  // flag
+  if (land && tid == 0 && *flag) {
+    // The acquire above made the records visible to this thread; the proxy
+    // fence extends that to its bulk copies.
+    fence_proxy_async_global();
+    uint32_t bytes = 0;
+    for (int i = 0; i < nparts; ++i) bytes += rec(i) >= 0 ? kPartFloats * 4 : 0;
+    mbar_arrive_expect_tx(land_bar, bytes);  // completes the phase at once when nothing is copied
+    for (int i = 0; i < nparts; ++i)
+      if (rec(i) >= 0)
+        bulk_load(landing + i * kPartFloats * 4, p.part_o + rec(i) * kPartFloats, kPartFloats * 4, land_bar);
+  }
   const int sp = warp & 3, mb = warp >> 2;
   const int de = 32 * sp + lane;  // dim inside the 128-dim block
-  if (*flag && tid < kHeads) {
-    // (m, l) of every part, eight parts' loads in flight at a time.
-    const int e = tid;
+  if (*flag && tid >= 64 && tid < 64 + kHeads) {
+    // (m, l) of every part, eight parts' loads in flight at a time (warps
+    // 2-3, beside thread 0's bulk copies).
+    const int e = tid - 64;
     float M = -INFINITY;
     for (int i0 = 0; i0 < nparts; i0 += 8) {
       float mv[8], lv[8];
@@ -256,12 +263,13 @@ __device__ bool merge_at_end(const Params& p, int t, int64_t total, int grid, in
         mv[k] = -INFINITY;
         lv[k] = 0.f;
         if (i < nparts) {
-          if (recs[i] < 0) {
+          const int64_t r = rec(i);
+          if (r < 0) {
             mv[k] = own_ml[2 * e];
             lv[k] = own_ml[2 * e + 1];
           } else {
-            mv[k] = __ldcg(p.part_ml + recs[i] * 2 * kHeads + 2 * e);
-            lv[k] = __ldcg(p.part_ml + recs[i] * 2 * kHeads + 2 * e + 1);
+            mv[k] = __ldcg(p.part_ml + r * 2 * kHeads + 2 * e);
+            lv[k] = __ldcg(p.part_ml + r * 2 * kHeads + 2 * e + 1);
           }
         }
       }
@@ -313,7 +321,7 @@ __device__ bool merge_at_end(const Params& p, int t, int64_t total, int grid, in
     if (land) {
       for (int i = 0; i < nparts; ++i) {
         float4 v[4];
-        if (recs[i] < 0) {
+        if (rec(i) < 0) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) v[q] = make_float4(own[4 * q], own[4 * q + 1], own[4 * q + 2], own[4 * q + 3]);
         } else {
@@ -329,8 +337,8 @@ __device__ bool merge_at_end(const Params& p, int t, int64_t total, int grid, in
 #pragma unroll
         for (int k = 0; k < kMergeBatch; ++k) {
           const int i = i0 + k;
-          if (i < nparts && recs[i] >= 0) {
-            const float4* src = reinterpret_cast<const float4*>(p.part_o + recs[i] * kPartFloats);
+          if (i < nparts && rec(i) >= 0) {
+            const float4* src = reinterpret_cast<const float4*>(p.part_o + rec(i) * kPartFloats);
 #pragma unroll
             for (int q = 0; q < 4; ++q) v[k][q] = __ldcg(src + part_index(mb, q, de));
           } else if (i < nparts) {
@@ -395,6 +403,7 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   int* q_last = reinterpret_cast<int*>(smem + kOffMisc + 32);      // last segment loaded per Q slot
   float* alpha_smem = reinterpret_cast<float*>(smem + kOffMisc + 64);   // 16
   float* ml_smem = reinterpret_cast<float*>(smem + kOffMisc + 128);     // 16 x (m, l)
+  MergeParts* mparts = reinterpret_cast<MergeParts*>(smem + kOffParts);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -631,6 +640,21 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     const int srow = 16 * sp + (lane & 15);  // S^T row held by this thread (lane < 16)
     float* red = sx;  // reduction scratch: tile maxima [2][4 warps][16 heads], row sums [4][16]
     const int h0 = (lane >> 4) * 8;           // first of this lane's 8 heads
+    {
+      // Record indices of the parts of this CTA's first and last tokens,
+      // worked out while the first tile is on its way (the merges at the
+      // end then start at once).  Read after the CTA's closing barrier.
+      const int slot = e >> 6, ip = e & 63;
+      const int tt = static_cast<int>((slot == 0 ? u0 : u0 + n - 1) / kTilesPerTok);
+      int c_lo, c_hi;
+      covering_ctas(tt, total, gridDim.x, c_lo, c_hi);
+      const int np = c_hi - c_lo + 1;
+      if (ip == 0) {
+        mparts->c_lo[slot] = c_lo;
+        mparts->nparts[slot] = np;
+      }
+      if (ip < np && ip < kMaxParts) mparts->rec[slot][ip] = part_record(tt, c_lo + ip, total, gridDim.x);
+    }
     float m_run[kHeads], l_row[8];
     int sg = -1, seg_first_tile = 0;
     int owed_t = -1, owed_tk = 0;  // (thread 0) a ticket taken whose part is not settled yet
@@ -895,7 +919,8 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
   uint32_t land_parity = 0;
   for (int k = 0; k < nmerge && k < 2; ++k) {
     if (k > 0) __syncthreads();  // the merge scratch (P and Sx buffers, free now) and landing are reused
-    if (merge_at_end(p, merge_list[1 + 2 * k], total, gridDim.x, merge_list[2 + 2 * k], ml_smem, tmem_base,
+    const int t = merge_list[1 + 2 * k];
+    if (merge_at_end(p, t, *mparts, t == t_first ? 0 : 1, merge_list[2 + 2 * k], ml_smem, tmem_base,
                      p_mem, stage_mem, land_bar, land_parity))
       land_parity ^= 1;
   }

@@ -504,7 +504,7 @@ constexpr int kTopK = DSA_TOPK;
 constexpr int kStageCap = 512;                        // staged keys per warp
 constexpr int kMergeOut = 4;                          // merge sort: outputs per thread per level
 constexpr int kStageTotal = kSelWarps * kStageCap;    // 16384
-constexpr size_t kSelSmem = sizeof(uint64_t) * (kTopK + kStageTotal) + sizeof(uint32_t) * kBins +
+constexpr size_t kSelSmem = sizeof(uint64_t) * (kTopK + kStageTotal) + sizeof(uint32_t) * 2 * kBins +
                             sizeof(int) * (32 + 8 + kSelWarps);
 
 struct SelectParams {
@@ -523,8 +523,11 @@ __device__ __forceinline__ uint64_t composite(float s, int tok) {
   return (static_cast<uint64_t>(score_key(s)) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(tok));
 }
 
-// Inclusive prefix sum over the 1024 threads of the block.
-__device__ __forceinline__ int block_scan_incl(int v, int* warp_tot) {
+// Inclusive prefix sum over the 1024 threads of the block; total receives
+// the block's sum.  One barrier: every warp scans the 32 warp totals itself.
+// warp_tot (32 ints) must not be written again until every thread has passed
+// a later barrier (each caller below has one before its next scan).
+__device__ __forceinline__ int block_scan_incl(int v, int* warp_tot, int& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -533,19 +536,15 @@ __device__ __forceinline__ int block_scan_incl(int v, int* warp_tot) {
   }
   if (lane == 31) warp_tot[warp] = v;
   __syncthreads();
-  if (warp == 0) {
-    int t = warp_tot[lane];
+  const int wt = warp_tot[lane];
+  int ti = wt;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int u = __shfl_up_sync(0xffffffffu, t, o);
-      if (lane >= o) t += u;
-    }
-    warp_tot[lane] = t;  // inclusive totals
+  for (int o = 1; o < 32; o <<= 1) {
+    int u = __shfl_up_sync(0xffffffffu, ti, o);
+    if (lane >= o) ti += u;
   }
-  __syncthreads();
-  const int add = warp > 0 ? warp_tot[warp - 1] : 0;
-  __syncthreads();
-  return v + add;
+  total = __shfl_sync(0xffffffffu, ti, 31);
+  return v + __shfl_sync(0xffffffffu, ti - wt, warp);
 }
 
 // Finds the bin d (scanning from the highest bin down) that holds the
@@ -557,7 +556,8 @@ __device__ __forceinline__ void find_bin(const uint32_t* hist, int need, int* wa
   if (t == 0) { res[0] = 0; res[1] = 0; res[2] = 0; }
   const int hi = kBins - 1 - 2 * t, lo = hi - 1;
   const int a = static_cast<int>(hist[hi]), c = static_cast<int>(hist[lo]);
-  const int incl = block_scan_incl(a + c, warp_tot);
+  int total;
+  const int incl = block_scan_incl(a + c, warp_tot, total);
   const int excl = incl - a - c;
   if (excl < need && need <= excl + a) { res[0] = hi; res[1] = excl; res[2] = a; }
   else if (excl + a < need && need <= incl) { res[0] = lo; res[1] = excl + a; res[2] = c; }
@@ -694,12 +694,12 @@ __device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp, uint32_t* cnt,
   // Thread t owns buckets 2t, 2t + 1: counts -> exclusive starts.
   const int c0 = static_cast<int>(cnt[2 * t]), c1 = static_cast<int>(cnt[2 * t + 1]);
   if (c0 > kBucketCap || c1 > kBucketCap) atomicOr(flag, 1);
-  const int incl = block_scan_incl(c0 + c1, warp_tot);  // its barriers order the reads above
+  int nvalid;
+  const int incl = block_scan_incl(c0 + c1, warp_tot, nvalid);
   cnt[2 * t] = incl - c0 - c1;
   cnt[2 * t + 1] = incl - c1;
-  __syncthreads();
+  __syncthreads();  // also orders the flag's atomics before its read
   if (*flag) return sort_desc_2048_merge(buf, tmp);
-  const int nvalid = warp_tot[31];
   if (v0) tmp[cnt[b0] + s0] = x0;
   if (v1) tmp[cnt[b1] + s1] = x1;
   __syncthreads();
@@ -725,7 +725,8 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
   uint64_t* sel = reinterpret_cast<uint64_t*>(smem_raw);
   uint64_t* stage = sel + kTopK;
   uint32_t* hist = reinterpret_cast<uint32_t*>(stage + kStageTotal);
-  int* warp_tot = reinterpret_cast<int*>(hist + kBins);  // 32 ints
+  uint32_t* hist2 = hist + kBins;                         // second-level histogram
+  int* warp_tot = reinterpret_cast<int*>(hist2 + kBins);  // 32 ints
   int* res = warp_tot + 32;                               // bin, above, count, overflow, nsel
   int* wcnt = res + 8;                                    // staged keys per warp
 
@@ -747,18 +748,20 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
   const int K = L < kTopK ? L : kTopK;
   const float4* row4 = reinterpret_cast<const float4*>(row);
   const int L4 = (L + 3) >> 2;  // float4s covering [0, L)
+  // The histogram the score kernel accumulated for this request, copied
+  // into shared memory ahead of the scores (no registers held meanwhile).
+  if (L > kTopK && tid < kBins / 4) cp_async16(smem_u32(hist + 4 * tid), ghist + 4 * tid);
   // The main pass's first scores need no threshold: their loads are in
-  // flight while the histogram is read and the boundary bin is found.
+  // flight while the boundary bin is found.
   float4 nv[4];
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     const int q = u * kSelThreads + tid;
     nv[u] = (L > kTopK && q < L4) ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-
-  // The histogram the score kernel accumulated for this request.
-  for (int i = tid; i < kBins; i += kSelThreads) hist[i] = ghist[i];
+  for (int i = tid; i < kBins; i += kSelThreads) hist2[i] = 0u;
   if (tid == 0) { res[3] = 0; res[4] = 0; res[5] = 0; }
+  cp_async_wait_all();
   __syncthreads();
 
   if (L <= kTopK) {
@@ -784,9 +787,6 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     if (thr != thr) thr = INFINITY;
     uint64_t* mine = stage + warp * kStageCap;
     int wcount = 0;
-    // find_bin has read the first-level histogram; it is rebuilt below as
-    // the second-level one (next 11 bits of the boundary bin).
-    for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
     // Loads run one round ahead of the compares, so the L2 latency of round
     // r + 1 overlaps the work on round r (round 0's were issued on entry).
     for (int q0 = 0; q0 < L4; q0 += 4 * kSelThreads) {
@@ -843,7 +843,10 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     if (staged) {
       // Scores of this warp's staged tokens, four independent loads in
       // flight per lane; keys of the boundary bin count into the histogram
-      // of the first refinement pass.
+      // of the first refinement pass (hist2: next 11 key bits).  Selecting
+      // the winners' scores from the main pass's registers instead measured
+      // slower: the longer-lived registers spill, and any load the loop
+      // waits on then waits behind the next round's score loads.
       const int avail = wcount;
       for (int j0 = lane; j0 < avail; j0 += 128) {
         int ti[4];
@@ -857,7 +860,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
           if (j0 + 32 * u < avail) {
             const uint64_t c = composite(sv[u], ti[u]);
             mine[j0 + 32 * u] = c;
-            if (static_cast<uint32_t>(c >> 53) == bin1) atomicAdd(&hist[(c >> 42) & 0x7FF], 1u);
+            if (static_cast<uint32_t>(c >> 53) == bin1) atomicAdd(&hist2[(c >> 42) & 0x7FF], 1u);
           }
         }
       }
@@ -866,7 +869,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     uint64_t prefix = static_cast<uint64_t>(bin1) << 53;
     uint64_t mask = static_cast<uint64_t>(0x7FF) << 53;
     // Refine the boundary: 11-bit digits of the remaining 53 key bits.  With
-    // the keys staged, the first pass's histogram was built above.
+    // the keys staged, the first pass's histogram (hist2) was built above.
     const int shifts[5] = {42, 31, 20, 9, 0};
     const int widths[5] = {11, 11, 11, 11, 9};
     for (int pass = 0; pass < 5 && count != need; ++pass) {
@@ -890,7 +893,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
         }
         __syncthreads();
       }
-      find_bin(hist, need, warp_tot, res);
+      find_bin(pass == 0 && staged ? hist2 : hist, need, warp_tot, res);
       prefix |= static_cast<uint64_t>(res[0]) << sh;
       mask |= dm << sh;
       need -= res[1];
@@ -904,7 +907,8 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
       const int avail = wcnt[warp];
       int cnt = 0;
       for (int j = lane; j < avail; j += 32) cnt += (area[j] & mask) >= prefix ? 1 : 0;
-      const int incl = block_scan_incl(cnt, warp_tot);
+      int total;
+      const int incl = block_scan_incl(cnt, warp_tot, total);
       int pos = incl - cnt;
       for (int j = lane; j < avail; j += 32) {
         const uint64_t c = area[j];

@@ -279,13 +279,15 @@ __device__ __forceinline__ uint64_t make_policy_evict_last() {
   return p;
 }
 
-// Orders this thread's generic-proxy shared-memory writes before later
-// async-proxy (tensor core / TMA) reads of the same bytes.
 // 16-byte global -> shared copy that bypasses L1 (cp.async.cg), with an L2
 // cache policy.  Completion is awaited with cp_async_wait_all().
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t policy) {
   asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;"
                ::"r"(dst), "l"(src), "l"(policy) : "memory");
+}
+// Same, default L2 policy.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
