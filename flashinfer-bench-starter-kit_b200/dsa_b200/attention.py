@@ -48,7 +48,6 @@ def _workspace_bytes(dev: torch.device, T: int) -> int:
     return n
 
 
-@torch.no_grad()
 def run(q_nope: torch.Tensor, q_pe: torch.Tensor, ckv_cache: torch.Tensor,
         kpe_cache: torch.Tensor, sparse_indices: torch.Tensor, sm_scale,
         output: torch.Tensor, lse: torch.Tensor) -> None:
