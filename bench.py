@@ -108,7 +108,10 @@ def profiled_traffic(kernel: str, workload: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling while the timed region runs."""
+    """nvidia-smi clock / throttle sampling while the timed region runs.  The
+    timed region starts only once the first sample has arrived (nvidia-smi
+    can take a second to start when every rank launches one), and at least
+    one sample taken after it ends is kept."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -116,33 +119,50 @@ class ClockSampler:
 
     def __init__(self, device: torch.device):
         self.proc = None
-        self.out = None
+        self.lines = []
+        self.reader = None
         try:
             uuid = str(torch.cuda.get_device_properties(device).uuid)
             uid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
             self.cmd = ["nvidia-smi", "-i", uid, f"--query-gpu={self.FIELDS}",
-                        "--format=csv,noheader,nounits", "-lms", "100"]
+                        "--format=csv,noheader,nounits", "-lms", "50"]
         except Exception:
             self.cmd = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
+
+    def _wait_lines(self, n, timeout):
+        t0 = time.perf_counter()
+        while len(self.lines) < n and time.perf_counter() - t0 < timeout:
+            time.sleep(0.01)
 
     def __enter__(self):
         if self.cmd:
             try:
                 self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE,
                                              stderr=subprocess.DEVNULL, text=True)
+                import threading
+                self.reader = threading.Thread(target=self._read, daemon=True)
+                self.reader.start()
+                self._wait_lines(1, 10.0)
             except OSError:
                 self.proc = None
-        time.sleep(0.3)
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            self._wait_lines(len(self.lines) + 1, 2.0)  # a sample taken after the region
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.out, _ = self.proc.communicate()
+                self.proc.wait()
+            if self.reader is not None:
+                self.reader.join(timeout=2)
+        self.out = "".join(self.lines)
 
     def summary(self):
         if not self.out:
