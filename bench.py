@@ -348,9 +348,10 @@ def main() -> int:
     value = total_bytes / (ms_step * 1e-3) / 1e9
 
     # ---- end to end through the public run() API with host buffers ----
-    e2e = None
+    e2e = e2e_graph = None
     if not args.no_e2e:
         e2e = end_to_end(step, dec, args, world, local_rank, total_bytes)
+        e2e_graph = end_to_end_graph(dec, args, world, local_rank, total_bytes)
 
     # ---- parity: outputs gathered to rank 0 and checked against the oracle ----
     parity = verify(step, dec, world, rank, dev)
@@ -395,6 +396,7 @@ def main() -> int:
         "cpu_baseline": cpu,
         "gpu_reference": gpu_ref,
         "e2e": e2e,
+        "e2e_graph": e2e_graph,
         "gpu_launches": 4 * K,  # histogram clear, score, select, attention kernels per step
         "clocks": clk.summary(),
         "verified": bool(parity.get("ok")),
@@ -421,6 +423,45 @@ def _arena(tensors, device=None, pinned=False):
     views = [buf[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape)
              for o, t in zip(offs, tensors)]
     return buf, views
+
+
+def end_to_end_graph(dec, args, world, local_rank, total_bytes):
+    """Same metric through the captured step with host I/O
+    (dsa_b200.pipeline.DecodeStep(host_io=True)): every step one graph launch
+    that copies the step's inputs in from pinned memory, runs indexer ->
+    attention and copies the outputs back, timed like end_to_end."""
+    import torch.distributed as dist
+
+    from dsa_b200 import pipeline
+
+    dev = dec.indexer.seq_lens.device
+    io = pipeline.DecodeStep(dec, use_graph=True, host_io=True)
+    comp = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        io.replay_io()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(comp)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        io.replay_io()
+    host_us = (time.perf_counter() - t0) / args.steps * 1e6
+    b.record(comp)
+    torch.cuda.synchronize()
+    ms = torch.tensor([a.elapsed_time(b) / args.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms)
+    out = {"value": total_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+           "h2d_bytes_per_step": io._in_host.numel(), "d2h_bytes_per_step": io._out_host.numel(),
+           "host_issue_us_per_step": host_us,
+           "api": "dsa_b200.pipeline.DecodeStep(host_io=True).replay_io(): one graph per step "
+                  "(pinned inputs in, indexer -> attention, outputs back)"}
+    del io
+    return out
 
 
 def end_to_end(step, dec, args, world, local_rank, total_bytes):

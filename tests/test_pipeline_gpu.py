@@ -45,3 +45,24 @@ def test_two_stream_graph_matches_one_stream(cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(topk, two.topk[lo:hi])
         assert torch.equal(out, two.out[lo:hi]) and torch.equal(lse, two.lse[lo:hi])
+
+
+def test_host_io_graph_matches_the_device_step(cuda_device):
+    """DecodeStep(host_io=True): one graph copies the pinned inputs in, runs the
+    step and copies the outputs back; results equal the device-resident step's
+    bit for bit, and inputs rewritten on the host reach the next replay."""
+    lens = [5000, 70000, 2049, 129, 0, 3000]
+    dec = workloads.make_decode_inputs(lens, seed=72, device=cuda_device)
+    ref = pipeline.DecodeStep(dec, use_graph=True)
+    io = pipeline.DecodeStep(dec, use_graph=True, host_io=True)
+    for new_len in (None, 4000):
+        if new_len is not None:
+            io.host_in[2][0] = new_len          # seq_lens, written on the host
+            dec.indexer.seq_lens[0] = new_len   # the same change for the device step
+        ref()
+        io.replay_io()
+        torch.cuda.synchronize()
+        topk, out, lse = io.host_out
+        assert torch.equal(topk, ref.topk.cpu())
+        assert torch.equal(out, ref.out.cpu()) and torch.equal(lse, ref.lse.cpu())
+    assert int((io.host_out[0][0] >= 0).sum()) == 2048
