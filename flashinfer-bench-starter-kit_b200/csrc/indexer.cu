@@ -96,7 +96,13 @@ constexpr int kOffBar = kOffScale + kScaleSlots * 2 * kScaleBytes; // 186368
 constexpr int kNumBars = 2 * kStages + 4 + 2 * kAccStages + kMmaWarps;
 constexpr int kOffMisc = kOffBar + 256;
 constexpr int kOffInfo = kOffMisc + 128;                          // producer warps x 32 tiles
-constexpr int kOffTiles = kOffInfo + kProdWarps * 32 * 5 * 4;
+// Weights and lengths of the first kWtReqs requests of a CTA's slice, staged
+// by the epilogue warps at the start: a request change then reads them from
+// shared memory instead of waiting on global loads with the pipeline behind it.
+constexpr int kWtReqs = 16;
+constexpr int kOffWts = kOffInfo + kProdWarps * 32 * 5 * 4;
+constexpr int kOffLens = kOffWts + kWtReqs * kHeads * 4;
+constexpr int kOffTiles = kOffLens + kWtReqs * 4;
 static_assert(kNumBars * 8 <= 256, "barrier area");
 static_assert(kStages % kProdWarps == 0 && kScaleSlots % kProdWarps == 0, "producer stride");
 static_assert(16 + 4 * (kThreads / 32) <= 128, "misc area");
@@ -397,6 +403,16 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
     // The score kernel is launched programmatically after the kernel that
     // clears the global histograms; only these warps touch them.
     griddep_wait();
+    float* w_smem = reinterpret_cast<float*>(smem + kOffWts);
+    int b_first = 0;
+    if (nt > 0) {
+      int j0 = 0;
+      locate(tile_off, p.batch, u0, b_first, j0);
+      const int nr = min(kWtReqs, p.batch - b_first);
+      for (int i = tid; i < nr * kHeads; i += 32 * kEpiWarps) w_smem[i] = __ldg(p.weights + b_first * kHeads + i);
+      if (tid < nr) reinterpret_cast<int*>(smem + kOffLens)[tid] = __ldg(p.seq_lens + b_first + tid);
+    }
+    named_barrier_sync(1, 32 * kEpiWarps);
     if (set < nt) {
       int b = 0, j = 0;
       locate(tile_off, p.batch, u0 + set, b, j);
@@ -405,10 +421,21 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
       float* srow = nullptr;
       float wt[kHeads];
       auto enter = [&]() {  // request b becomes current
-        L = clamp_len(__ldg(p.seq_lens + b), max_len, p.status);
+        const bool staged = b - b_first < kWtReqs;
+        L = clamp_len(staged ? reinterpret_cast<const int*>(smem + kOffLens)[b - b_first] : __ldg(p.seq_lens + b),
+                      max_len, p.status);
         srow = p.scores + static_cast<int64_t>(b) * p.score_stride;
+        if (staged) {
+          const float4* w4 = reinterpret_cast<const float4*>(w_smem + (b - b_first) * kHeads);
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) wt[h] = __ldg(p.weights + b * kHeads + h);
+          for (int h = 0; h < kHeads / 4; ++h) {
+            const float4 x = w4[h];
+            wt[4 * h] = x.x; wt[4 * h + 1] = x.y; wt[4 * h + 2] = x.z; wt[4 * h + 3] = x.w;
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) wt[h] = __ldg(p.weights + b * kHeads + h);
+        }
       };
       // Adds the warp's counts (request fb) into the global histogram.
       auto flush = [&](int fb) {
