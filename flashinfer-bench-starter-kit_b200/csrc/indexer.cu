@@ -525,14 +525,17 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
 }
 
 // ------------------------------------------------------------ top-k select
-constexpr int kSelThreads = 1024;
-constexpr int kSelWarps = kSelThreads / 32;
+// The select runs with T = 1024 threads per CTA (one CTA per SM: a batch
+// that fits the SMs in one wave is latency-bound) or T = 512 (two CTAs per
+// SM, for batches of more rows than SMs, where the select is throughput-bound).
 constexpr int kTopK = DSA_TOPK;
 constexpr int kStageCap = 512;                        // staged keys per warp
 constexpr int kMergeOut = 4;                          // merge sort: outputs per thread per level
-constexpr int kStageTotal = kSelWarps * kStageCap;    // 16384
-constexpr size_t kSelSmem = sizeof(uint64_t) * (kTopK + kStageTotal) + sizeof(uint32_t) * 2 * kBins +
-                            sizeof(int) * (32 + 8 + kSelWarps);
+template <int T>
+constexpr size_t sel_smem() {
+  return sizeof(uint64_t) * (kTopK + (T / 32) * kStageCap) + sizeof(uint32_t) * 2 * kBins +
+         sizeof(int) * (32 + 8 + T / 32);
+}
 
 struct SelectParams {
   const float* scores;
@@ -550,10 +553,11 @@ __device__ __forceinline__ uint64_t composite(float s, int tok) {
   return (static_cast<uint64_t>(score_key(s)) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(tok));
 }
 
-// Inclusive prefix sum over the 1024 threads of the block; total receives
-// the block's sum.  One barrier: every warp scans the 32 warp totals itself.
+// Inclusive prefix sum over the T threads of the block; total receives the
+// block's sum.  One barrier: every warp scans the T / 32 warp totals itself.
 // warp_tot (32 ints) must not be written again until every thread has passed
 // a later barrier (each caller below has one before its next scan).
+template <int T>
 __device__ __forceinline__ int block_scan_incl(int v, int* warp_tot, int& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -563,7 +567,7 @@ __device__ __forceinline__ int block_scan_incl(int v, int* warp_tot, int& total)
   }
   if (lane == 31) warp_tot[warp] = v;
   __syncthreads();
-  const int wt = warp_tot[lane];
+  const int wt = lane < T / 32 ? warp_tot[lane] : 0;
   int ti = wt;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -576,18 +580,29 @@ __device__ __forceinline__ int block_scan_incl(int v, int* warp_tot, int& total)
 
 // Finds the bin d (scanning from the highest bin down) that holds the
 // need-th largest element; res = {d, count strictly above d, hist[d]}.
+// Thread t holds the kBins / T bins kBins - 1 - (kBins / T) t - k, k = 0, 1, ...
+template <int T>
 __device__ __forceinline__ void find_bin(const uint32_t* hist, int need, int* warp_tot, int* res) {
+  constexpr int kPer = kBins / T;
   const int t = threadIdx.x;
   // Defined even if the histogram holds fewer than `need` keys (it cannot
   // when it matches the scores; the output stage checks every token).
   if (t == 0) { res[0] = 0; res[1] = 0; res[2] = 0; }
-  const int hi = kBins - 1 - 2 * t, lo = hi - 1;
-  const int a = static_cast<int>(hist[hi]), c = static_cast<int>(hist[lo]);
+  const int top = kBins - 1 - kPer * t;
+  int c[kPer];
+  int sum = 0;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    c[k] = static_cast<int>(hist[top - k]);
+    sum += c[k];
+  }
   int total;
-  const int incl = block_scan_incl(a + c, warp_tot, total);
-  const int excl = incl - a - c;
-  if (excl < need && need <= excl + a) { res[0] = hi; res[1] = excl; res[2] = a; }
-  else if (excl + a < need && need <= incl) { res[0] = lo; res[1] = excl + a; res[2] = c; }
+  int excl = block_scan_incl<T>(sum, warp_tot, total) - sum;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    if (excl < need && need <= excl + c[k]) { res[0] = top - k; res[1] = excl; res[2] = c[k]; }
+    excl += c[k];
+  }
   __syncthreads();
 }
 
@@ -614,13 +629,18 @@ __device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int m) {
 }
 
 // Descending sort of the 2048 keys in buf (tmp: 2048 more slots), for any
-// key distribution.  Each warp sorts 64 keys in registers (bitonic, 2 per lane); then five
-// merge-path levels merge runs of 64, 128, ... 1024 keys.  Every thread of
-// the block must call it; returns the buffer that holds the result.
+// key distribution.  Each warp sorts runs of 64 keys in registers (bitonic,
+// 2 per lane; kTopK / (2 T) runs per warp); then five merge-path levels merge
+// runs of 64, 128, ... 1024 keys with 512 threads.  Every thread of the block
+// must call it; returns the buffer that holds the result.
+template <int T>
 __device__ uint64_t* sort_desc_2048_merge(uint64_t* buf, uint64_t* tmp) {
   const int t = threadIdx.x;
   const int lane = t & 31;
-  uint64_t x0 = buf[2 * t], x1 = buf[2 * t + 1];
+#pragma unroll 1
+  for (int half = 0; half < kTopK / (2 * T); ++half) {
+  uint64_t* run = buf + half * 2 * T;
+  uint64_t x0 = run[2 * t], x1 = run[2 * t + 1];
 #pragma unroll
   for (int kk = 1; kk <= 6; ++kk) {
     const int k = 1 << kk;
@@ -639,9 +659,10 @@ __device__ uint64_t* sort_desc_2048_merge(uint64_t* buf, uint64_t* tmp) {
       }
     }
   }
+  *reinterpret_cast<ulonglong2*>(run + 2 * t) = make_ulonglong2(x0, x1);
+  }
   uint64_t* src = buf;
   uint64_t* dst = tmp;
-  *reinterpret_cast<ulonglong2*>(src + 2 * t) = make_ulonglong2(x0, x1);
   __syncthreads();
   // Merge levels: kMergeOut consecutive outputs per thread, so one binary
   // search (merge-path split) per kMergeOut outputs.
@@ -693,65 +714,90 @@ __device__ uint64_t* sort_desc_2048_merge(uint64_t* buf, uint64_t* tmp) {
 // must call it; returns the buffer that holds the result.
 constexpr int kBucketCap = 48;
 
+template <int T>
 __device__ uint64_t* sort_desc_2048(uint64_t* buf, uint64_t* tmp, uint32_t* cnt, int* warp_tot,
                                     uint32_t* scratch, int* flag) {
+  constexpr int K = kTopK / T;  // keys per thread (consecutive), and buckets per thread
   const int t = threadIdx.x;
   const int lane = t & 31;
   const int warp = t >> 5;
-  const ulonglong2 xx = *reinterpret_cast<const ulonglong2*>(buf + 2 * t);
-  const uint64_t x0 = xx.x, x1 = xx.y;
-  const bool v0 = x0 != 0, v1 = x1 != 0;
-  const uint32_t h0 = static_cast<uint32_t>(x0 >> 32), h1 = static_cast<uint32_t>(x1 >> 32);
-  uint32_t mx = __reduce_max_sync(0xffffffffu, max(v0 ? h0 : 0u, v1 ? h1 : 0u));
-  uint32_t mn = __reduce_min_sync(0xffffffffu, min(v0 ? h0 : 0xFFFFFFFFu, v1 ? h1 : 0xFFFFFFFFu));
+  uint64_t x[K];
+  bool v[K];
+#pragma unroll
+  for (int k = 0; k < K; k += 2) {
+    const ulonglong2 xx = *reinterpret_cast<const ulonglong2*>(buf + K * t + k);
+    x[k] = xx.x;
+    x[k + 1] = xx.y;
+  }
+  uint32_t hmax = 0u, hmin = 0xFFFFFFFFu;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    v[k] = x[k] != 0;
+    const uint32_t h = static_cast<uint32_t>(x[k] >> 32);
+    hmax = max(hmax, v[k] ? h : 0u);
+    hmin = min(hmin, v[k] ? h : 0xFFFFFFFFu);
+  }
+  uint32_t mx = __reduce_max_sync(0xffffffffu, hmax);
+  uint32_t mn = __reduce_min_sync(0xffffffffu, hmin);
   if (lane == 0) { scratch[warp] = mx; scratch[32 + warp] = mn; }
-  cnt[t] = 0;
-  cnt[t + 1024] = 0;
+  for (int i = t; i < kTopK; i += T) cnt[i] = 0;
   __syncthreads();
-  mx = __reduce_max_sync(0xffffffffu, scratch[lane]);
-  mn = __reduce_min_sync(0xffffffffu, scratch[32 + lane]);
+  mx = __reduce_max_sync(0xffffffffu, lane < T / 32 ? scratch[lane] : 0u);
+  mn = __reduce_min_sync(0xffffffffu, lane < T / 32 ? scratch[32 + lane] : 0xFFFFFFFFu);
   if (mx < mn) return buf;  // no non-zero keys
   const uint32_t span = mx - mn;
   const int shift = span < 2048 ? 0 : 32 - __clz(static_cast<int>(span)) - 11;
-  const int b0 = 2047 - static_cast<int>((h0 - mn) >> shift);
-  const int b1 = 2047 - static_cast<int>((h1 - mn) >> shift);
-  const int s0 = v0 ? static_cast<int>(atomicAdd(&cnt[b0], 1u)) : 0;
-  const int s1 = v1 ? static_cast<int>(atomicAdd(&cnt[b1], 1u)) : 0;
+  int bk[K], sl[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    bk[k] = v[k] ? 2047 - static_cast<int>((static_cast<uint32_t>(x[k] >> 32) - mn) >> shift) : 0;
+    sl[k] = v[k] ? static_cast<int>(atomicAdd(&cnt[bk[k]], 1u)) : 0;
+  }
   __syncthreads();
-  // Thread t owns buckets 2t, 2t + 1: counts -> exclusive starts.
-  const int c0 = static_cast<int>(cnt[2 * t]), c1 = static_cast<int>(cnt[2 * t + 1]);
-  if (c0 > kBucketCap || c1 > kBucketCap) atomicOr(flag, 1);
+  // Thread t owns buckets K t .. K t + K - 1: counts -> exclusive starts.
+  int c[K];
+  int sum = 0;
+  bool over = false;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    c[k] = static_cast<int>(cnt[K * t + k]);
+    sum += c[k];
+    over = over || c[k] > kBucketCap;
+  }
+  if (over) atomicOr(flag, 1);
   int nvalid;
-  const int incl = block_scan_incl(c0 + c1, warp_tot, nvalid);
-  cnt[2 * t] = incl - c0 - c1;
-  cnt[2 * t + 1] = incl - c1;
+  int run = block_scan_incl<T>(sum, warp_tot, nvalid) - sum;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    cnt[K * t + k] = run;
+    run += c[k];
+  }
   __syncthreads();  // also orders the flag's atomics before its read
-  if (*flag) return sort_desc_2048_merge(buf, tmp);
-  if (v0) tmp[cnt[b0] + s0] = x0;
-  if (v1) tmp[cnt[b1] + s1] = x1;
+  if (*flag) return sort_desc_2048_merge<T>(buf, tmp);
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+    if (v[k]) tmp[cnt[bk[k]] + sl[k]] = x[k];
   __syncthreads();
   // Rank inside the bucket; the zero keys at buf[nvalid..] are not touched.
-  if (v0) {
-    const int st = cnt[b0], en = b0 < 2047 ? static_cast<int>(cnt[b0 + 1]) : nvalid;
-    int r = 0;
-    for (int j = st; j < en; ++j) r += tmp[j] > x0 ? 1 : 0;
-    buf[st + r] = x0;
-  }
-  if (v1) {
-    const int st = cnt[b1], en = b1 < 2047 ? static_cast<int>(cnt[b1 + 1]) : nvalid;
-    int r = 0;
-    for (int j = st; j < en; ++j) r += tmp[j] > x1 ? 1 : 0;
-    buf[st + r] = x1;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    if (v[k]) {
+      const int st = cnt[bk[k]], en = bk[k] < 2047 ? static_cast<int>(cnt[bk[k] + 1]) : nvalid;
+      int r = 0;
+      for (int j = st; j < en; ++j) r += tmp[j] > x[k] ? 1 : 0;
+      buf[st + r] = x[k];
+    }
   }
   __syncthreads();
   return buf;
 }
 
-__global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const SelectParams p) {
+template <int T>
+__global__ void __launch_bounds__(T, 1024 / T) topk_select_kernel(const SelectParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint64_t* sel = reinterpret_cast<uint64_t*>(smem_raw);
   uint64_t* stage = sel + kTopK;
-  uint32_t* hist = reinterpret_cast<uint32_t*>(stage + kStageTotal);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(stage + (T / 32) * kStageCap);
   uint32_t* hist2 = hist + kBins;                         // second-level histogram
   int* warp_tot = reinterpret_cast<int*>(hist2 + kBins);  // 32 ints
   int* res = warp_tot + 32;                               // bin, above, count, overflow, nsel
@@ -783,19 +829,19 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
   float4 nv[4];
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
-    const int q = u * kSelThreads + tid;
+    const int q = u * T + tid;
     nv[u] = (L > kTopK && q < L4) ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  for (int i = tid; i < kBins; i += kSelThreads) hist2[i] = 0u;
+  for (int i = tid; i < kBins; i += T) hist2[i] = 0u;
   if (tid == 0) { res[3] = 0; res[4] = 0; res[5] = 0; }
   cp_async_wait_all();
   __syncthreads();
 
   if (L <= kTopK) {
-    for (int i = tid; i < kTopK; i += kSelThreads) sel[i] = i < L ? composite(row[i], i) : 0ull;
+    for (int i = tid; i < kTopK; i += T) sel[i] = i < L ? composite(row[i], i) : 0ull;
     __syncthreads();
   } else {
-    find_bin(hist, K, warp_tot, res);
+    find_bin<T>(hist, K, warp_tot, res);
     const uint32_t bin1 = static_cast<uint32_t>(res[0]);
     int need = K - res[1];
     int count = res[2];
@@ -816,12 +862,12 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
     int wcount = 0;
     // Loads run one round ahead of the compares, so the L2 latency of round
     // r + 1 overlaps the work on round r (round 0's were issued on entry).
-    for (int q0 = 0; q0 < L4; q0 += 4 * kSelThreads) {
+    for (int q0 = 0; q0 < L4; q0 += 4 * T) {
       float4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         v[u] = nv[u];
-        const int q = q0 + (4 + u) * kSelThreads + tid;
+        const int q = q0 + (4 + u) * T + tid;
         nv[u] = q < L4 ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       uint32_t msk = 0;
@@ -832,10 +878,10 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
         msk |= (!(v[u].z < thr) ? 4u : 0u) << (4 * u);
         msk |= (!(v[u].w < thr) ? 8u : 0u) << (4 * u);
       }
-      if (q0 + 4 * kSelThreads > L4 - 1) {  // last round: drop positions >= L
+      if (q0 + 4 * T > L4 - 1) {  // last round: drop positions >= L
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int i0 = 4 * (q0 + u * kSelThreads + tid);
+          const int i0 = 4 * (q0 + u * T + tid);
           const int nv = L - i0;
           const uint32_t keep = nv >= 4 ? 0xFu : (nv > 0 ? (1u << nv) - 1u : 0u);
           msk &= ~(0xFu << (4 * u)) | (keep << (4 * u));
@@ -854,7 +900,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
         while (msk) {
           const int bit = __ffs(msk) - 1;
           msk &= msk - 1;
-          const int i = 4 * (q0 + (bit >> 2) * kSelThreads + tid) + (bit & 3);
+          const int i = 4 * (q0 + (bit >> 2) * T + tid) + (bit & 3);
           if (pos < kStageCap) mine[pos] = static_cast<uint64_t>(i);
           ++pos;
         }
@@ -903,7 +949,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
       const int sh = shifts[pass];
       const uint64_t dm = (static_cast<uint64_t>(1) << widths[pass]) - 1;
       if (pass > 0 || !staged) {
-        for (int i = tid; i < kBins; i += kSelThreads) hist[i] = 0;
+        for (int i = tid; i < kBins; i += T) hist[i] = 0;
         __syncthreads();
         if (staged) {
           const uint64_t* area = stage + warp * kStageCap;
@@ -913,14 +959,14 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
             if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
           }
         } else {
-          for (int i = tid; i < L; i += kSelThreads) {
+          for (int i = tid; i < L; i += T) {
             const uint64_t c = composite(row[i], i);
             if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
           }
         }
         __syncthreads();
       }
-      find_bin(pass == 0 && staged ? hist2 : hist, need, warp_tot, res);
+      find_bin<T>(pass == 0 && staged ? hist2 : hist, need, warp_tot, res);
       prefix |= static_cast<uint64_t>(res[0]) << sh;
       mask |= dm << sh;
       need -= res[1];
@@ -935,7 +981,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
       int cnt = 0;
       for (int j = lane; j < avail; j += 32) cnt += (area[j] & mask) >= prefix ? 1 : 0;
       int total;
-      const int incl = block_scan_incl(cnt, warp_tot, total);
+      const int incl = block_scan_incl<T>(cnt, warp_tot, total);
       int pos = incl - cnt;
       for (int j = lane; j < avail; j += 32) {
         const uint64_t c = area[j];
@@ -946,7 +992,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
       }
     } else {
       const int Lr = (L + 31) & ~31;
-      for (int i = tid; i < Lr; i += kSelThreads) {
+      for (int i = tid; i < Lr; i += T) {
         const bool in = i < L;
         const uint64_t c = in ? composite(row[i], i) : 0ull;
         warp_append(in && (c & mask) >= prefix, c, sel, &res[4], kTopK);
@@ -956,11 +1002,11 @@ __global__ void __launch_bounds__(kSelThreads, 1) topk_select_kernel(const Selec
   }
 
   const uint64_t* sorted =
-      sort_desc_2048(sel, stage, hist, warp_tot, reinterpret_cast<uint32_t*>(stage + kTopK), &res[5]);
+      sort_desc_2048<T>(sel, stage, hist, warp_tot, reinterpret_cast<uint32_t*>(stage + kTopK), &res[5]);
 
   int32_t* out = p.out + static_cast<int64_t>(b) * kTopK;
   const int32_t* bt = p.block_table + static_cast<int64_t>(bt_row < 0 ? 0 : bt_row) * p.max_pages;
-  for (int i = tid; i < kTopK; i += kSelThreads) {
+  for (int i = tid; i < kTopK; i += T) {
     int32_t v = -1;
     if (i < K) {
       const int tok = static_cast<int>(~static_cast<uint32_t>(sorted[i]));
@@ -985,11 +1031,13 @@ int launch_topk_select(const float* scores, const unsigned int* hist, const int3
                        const int32_t* block_table, const int32_t* row_req, int32_t* out, int rows,
                        int score_stride, int max_pages, unsigned int* status, const DeviceInfo& info,
                        cudaStream_t s) {
-  if (ix::kSelSmem > info.max_smem_optin) return DSA_ERR_UNSUPPORTED_DEVICE;
+  if (ix::sel_smem<1024>() > info.max_smem_optin) return DSA_ERR_UNSUPPORTED_DEVICE;
   std::call_once(ix::g_sel_attr_once[info.device], [&]() {
     ix::g_sel_attr_status[info.device] =
-        cudaFuncSetAttribute(ix::topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(ix::kSelSmem)) == cudaSuccess
+        cudaFuncSetAttribute(ix::topk_select_kernel<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(ix::sel_smem<1024>())) == cudaSuccess &&
+                cudaFuncSetAttribute(ix::topk_select_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(ix::sel_smem<512>())) == cudaSuccess
             ? DSA_OK
             : DSA_ERR_CUDA;
   });
@@ -1004,9 +1052,15 @@ int launch_topk_select(const float* scores, const unsigned int* hist, const int3
   selp.out = out;
   selp.score_stride = score_stride;
   selp.max_pages = max_pages;
-  if (launch_programmatic(ix::topk_select_kernel, dim3(rows), dim3(ix::kSelThreads), ix::kSelSmem, s,
-                          selp) != cudaSuccess)
-    return DSA_ERR_CUDA;
+  // One 1024-thread CTA per row while the rows fit the SMs in one wave (the
+  // select is then a latency chain per row); more rows than SMs run two
+  // 512-thread CTAs per SM, where the select is throughput-bound.
+  const cudaError_t e =
+      rows > info.num_sms
+          ? launch_programmatic(ix::topk_select_kernel<512>, dim3(rows), dim3(512), ix::sel_smem<512>(), s, selp)
+          : launch_programmatic(ix::topk_select_kernel<1024>, dim3(rows), dim3(1024), ix::sel_smem<1024>(), s,
+                                selp);
+  if (e != cudaSuccess) return DSA_ERR_CUDA;
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
   return DSA_OK;
 }
@@ -1045,7 +1099,7 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
   int st = current_device_info(&info);
   if (st != DSA_OK) return st;
   const size_t smem1 = ix::score_smem_bytes(batch);
-  if (smem1 > info.max_smem_optin || ix::kSelSmem > info.max_smem_optin)
+  if (smem1 > info.max_smem_optin || ix::sel_smem<1024>() > info.max_smem_optin)
     return DSA_ERR_UNSUPPORTED_DEVICE;
   std::call_once(ix::g_attr_once[info.device], [&]() {
     bool ok = cudaFuncSetAttribute(ix::indexer_score_kernel,

@@ -222,3 +222,27 @@ def test_workspace_reuse_across_sizes(cuda_device):
                                        max_pages=100)
     first = run_gpu(ix)
     assert torch.equal(first, run_gpu(ix))
+
+
+def test_select_wide_and_narrow_ctas_agree(cuda_device):
+    """More rows than SMs run the select as 512-thread CTAs (two per SM); at most
+    one row per SM as 1024-thread CTAs.  A row's result does not depend on which
+    variant ran it: degenerate rows (all scores equal, so the staging areas
+    overflow and the winners crowd one bucket) and rows of <= 2048 tokens
+    included."""
+    n_sm = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    B = n_sm + 20
+    g = torch.Generator().manual_seed(95)
+    lens = workloads.uniform_lengths(B, 2049, 40000, g)
+    lens[1], lens[7], lens[n_sm + 2] = 2048, 300, 0
+    ix = workloads.make_indexer_inputs(lens, pool_pages=1024, seed=96, device=cuda_device)
+    for r in (3, n_sm + 5):
+        ix.q_index_fp8[r].zero_()  # every score of the row is 0
+    wide = run_gpu(ix)  # B > SMs: 512-thread CTAs
+    for lo, hi in ((0, n_sm), (n_sm - 10, B)):
+        narrow = torch.full((hi - lo, 2048), 7, dtype=torch.int32, device=cuda_device)
+        indexer.run(ix.q_index_fp8[lo:hi], ix.k_index_cache_fp8, ix.weights[lo:hi], ix.seq_lens[lo:hi],
+                    ix.block_table[lo:hi], narrow)
+        torch.cuda.synchronize()
+        assert torch.equal(narrow, wide[lo:hi]), (lo, hi)
+    oracle_check(ix, wide, rows=[0, 1, 3, 7, n_sm + 2, n_sm + 5, B - 1])
