@@ -658,6 +658,10 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
     float m_run[kHeads], l_row[8];
     int sg = -1, seg_first_tile = 0;
     int owed_t = -1, owed_tk = 0;  // (thread 0) a ticket taken whose part is not settled yet
+    // A part written at a segment end whose publication waits for the next
+    // tile's first barrier: by then its stores have long completed, so the
+    // fence that orders them before the count no longer stalls the group.
+    int pub_t = -1;
     bool ok = true;
     int i = 0;
     for (; i < n; ++i) {
@@ -695,7 +699,13 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
       bool need = false;
 #pragma unroll
       for (int hh = 0; hh < kHeads; ++hh) need |= x[hh] > m_run[hh] + kRescaleThreshold;
-      if (named_barrier_or(1, 128, need || !ok)) {
+      if (pub_t >= 0) __threadfence();
+      const bool slow = named_barrier_or(1, 128, need || !ok);
+      if (pub_t >= 0) {
+        if (e == 0) atomicAdd(p.tok_pub + pub_t, 1);
+        pub_t = -1;
+      }
+      if (slow) {
         // ---- slow path: a wait gave up, or the running max moves.
         if (!named_barrier_and(1, 128, ok)) break;
         // Per-head tile max: a warp max (redux on order-preserving keys),
@@ -820,7 +830,9 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             p.lse[static_cast<int64_t>(t) * kHeads + e] = l > 0.f ? ml_smem[2 * e] + log2f(l) : -INFINITY;
           }
         } else {
-          const int parts = parts_of(t, total, gridDim.x);
+          const int slot = t == static_cast<int>(u0 / kTilesPerTok) ? 0 : 1;
+          const int parts = mparts->nparts[slot];
+          const int own = static_cast<int>(blockIdx.x) - mparts->c_lo[slot];
           const int tk = *ticket_smem;
           if (tk >= parts) {
             // The counter was not zero on entry.  This kernel leaves every
@@ -833,8 +845,8 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
             if (e == 0) atomicOr(p.status, DSA_DEV_STALE_WORKSPACE);
           } else if (tk < parts - 1 || i != n - 1) {
             // Publish this part: O^T in fp32 as this thread holds it, then
-            // (m, l); the fence orders them before the publication count.
-            const int64_t rec = part_record(t, blockIdx.x, total, gridDim.x);
+            // (m, l); a fence orders them before the publication count.
+            const int64_t rec = own < kMaxParts ? mparts->rec[slot][own] : part_record(t, blockIdx.x, total, gridDim.x);
             float4* po = reinterpret_cast<float4*>(p.part_o + rec * kPartFloats);
 #pragma unroll
             for (int mb = 0; mb < 4; ++mb) {
@@ -849,17 +861,19 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
               p.part_ml[rec * 2 * kHeads + 2 * e] = ml_smem[2 * e];
               p.part_ml[rec * 2 * kHeads + 2 * e + 1] = ml_smem[2 * e + 1];
             }
-            __threadfence();
-            named_barrier_sync(1, 128);
-            if (e == 0) {
-              atomicAdd(p.tok_pub + t, 1);
-              // The last arriver at its first segment (its O buffer is
-              // reused later) merges from records once its work is done.
-              if (tk == parts - 1) {
-                merge_list[1 + 2 * merge_list[0]] = t;
-                merge_list[2 + 2 * merge_list[0]] = -1;
-                ++merge_list[0];
-              }
+            if (i == n - 1) {  // nothing follows: publish now
+              __threadfence();
+              named_barrier_sync(1, 128);
+              if (e == 0) atomicAdd(p.tok_pub + t, 1);
+            } else {
+              pub_t = t;
+            }
+            // The last arriver at its first segment (its O buffer is reused
+            // later) merges from records once its work is done.
+            if (e == 0 && tk == parts - 1) {
+              merge_list[1 + 2 * merge_list[0]] = t;
+              merge_list[2 + 2 * merge_list[0]] = -1;
+              ++merge_list[0];
             }
           } else if (e == 0) {
             // The last arriver at its last segment: its part stays in TMEM
@@ -876,6 +890,12 @@ attention_kernel(const __grid_constant__ CUtensorMap ckv_map,
         named_barrier_sync(1, 128);
         if (e == 0) mbar_arrive(&o_empty[sg & 1]);
       }
+    }
+    if (pub_t >= 0) {
+      // The loop stopped before the deferred publication: publish now.
+      __threadfence();
+      named_barrier_sync(1, 128);
+      if (e == 0) atomicAdd(p.tok_pub + pub_t, 1);
     }
     if (i < n && e == 0) {
       // The CTA aborted at tile i.  Its output is void (the status word says
