@@ -39,8 +39,8 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // (row_req == nullptr: row b; a negative entry yields an all -1 row).
 int launch_topk_select(const float* scores, const unsigned int* hist, const int32_t* seq_lens,
                        const int32_t* block_table, const int32_t* row_req, int32_t* out, int rows,
-                       int score_stride, int max_pages, unsigned int* status, const DeviceInfo& info,
-                       cudaStream_t s);
+                       int score_stride, int max_pages, unsigned int* status, unsigned int* ready,
+                       const DeviceInfo& info, cudaStream_t s);
 
 // Launches `kernel` on `stream` with programmatic stream serialization, so
 // its CTAs may be scheduled while the previous kernel on the stream drains

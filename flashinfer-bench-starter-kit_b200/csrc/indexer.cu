@@ -82,6 +82,14 @@ constexpr int kBins = 2048;                               // radix bins: top 11 
 // 2047 tiles < 65536, so a counter never carries into its neighbour.
 constexpr int kFlushEvery = 2047;
 constexpr int kMaxBatch = 4096;
+// Per-request ready counters at the front of the workspace, at fixed offsets
+// for every request index a call can have, so that a later call (of any
+// batch) never takes histogram or score bytes for counters.  They are never
+// reset: the score kernel adds each request's (tile, epilogue warp) pairs to
+// [2 b] as they are scored, and the select, which waits until [2 b] - [2 b + 1]
+// reaches the request's count, advances [2 b + 1] by that count.  A zero-filled
+// workspace starts them consistent.
+constexpr size_t kReadyBytes = sizeof(unsigned int) * 2 * kMaxBatch;
 constexpr int kMaxPagesPerSeq = 1 << 20;
 constexpr int64_t kMaxPool = (int64_t(1) << 31) / kPageRows - 1;
 
@@ -121,6 +129,10 @@ struct ScoreParams {
   float* scores;          // [batch][score_stride]
   unsigned int* hist;     // [batch][kBins], cleared by hist_clear_kernel at every call
   unsigned int* status;
+  // [kMaxBatch][2]: per request, the count of scored (tile, epilogue warp)
+  // pairs and the count the select has consumed; never reset (see
+  // kReadyBytes).
+  unsigned int* ready;
   int64_t num_pages;
   int batch;
   int max_pages;
@@ -451,8 +463,16 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         }
         __syncwarp();
       };
+      // This warp's scored tiles of request fb count towards its ready count
+      // once its score stores and histogram flush are visible (release).
+      auto mark_ready = [&](int fb, int cnt) {
+        __threadfence();
+        __syncwarp();
+        if (lane == 0 && cnt > 0) atomicAdd(p.ready + 2 * fb, static_cast<unsigned int>(cnt));
+      };
       enter();
       int a = set, slot = set, since = 0;  // accumulator, scale slot of tile n
+      int scored = 0;                       // tiles of request b this warp has scored
       uint32_t aph = 0;
       for (int n = set; n < nt; n += 2) {
         const int tok = j * kTileTok + row;
@@ -500,9 +520,12 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         if ((a += 2) >= kAccStages) { a -= kAccStages; aph ^= 1; }
         if ((slot += 2) >= kScaleSlots) slot -= kScaleSlots;
         ++since;
+        ++scored;
         if (n + 2 < nt) {
           if ((j += 2) >= ntb) {
             flush(b);
+            mark_ready(b, scored);
+            scored = 0;
             since = 0;
             do { j -= ntb; ++b; ntb = tile_off[b + 1] - tile_off[b]; } while (j >= ntb);
             enter();
@@ -513,6 +536,7 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         }
       }
       flush(b);
+      mark_ready(b, scored);
     }
   }
 
@@ -545,6 +569,9 @@ struct SelectParams {
   const int32_t* seq_lens;
   const int32_t* block_table;
   int32_t* out;
+  // The score kernel's per-request ready counts ([2 b] scored, [2 b + 1]
+  // consumed), or nullptr: wait for the whole score grid instead.
+  unsigned int* ready;
   int score_stride;
   int max_pages;
 };
@@ -808,14 +835,32 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_select_kernel(const SelectPa
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int max_len = p.max_pages * kPage;
-  // Launched programmatically after the score kernel: nothing in global
-  // memory is touched before that grid has completed.
-  griddep_wait();
+  // Launched programmatically after the score kernel.  Without ready counts
+  // nothing in global memory is touched before that grid has completed; with
+  // them, a row's scores and histogram are read once its own request's
+  // tiles are scored (the counts are released after the stores they cover).
+  if (p.ready == nullptr) griddep_wait();
   griddep_launch_dependents();
   int L = __ldg(p.seq_lens + b);
   L = L < 0 ? 0 : (L > max_len ? max_len : L);  // the score kernel flags bad lengths
   const int bt_row = p.row_req ? __ldg(p.row_req + b) : b;
   if (bt_row < 0) L = 0;  // a row outside every request: all -1
+  if (p.ready != nullptr) {
+    if (tid == 0) {
+      // Each of the request's tiles is scored by four epilogue warps.
+      const unsigned int need = 4u * static_cast<unsigned int>((L + kTileTok - 1) / kTileTok);
+      const unsigned int base = p.ready[2 * b + 1];
+      const bool ok = wait_count_since(p.ready + 2 * b, base, need, p.status, kWaitLimitNs);
+      // The consumed count moves past this call's tiles; after a timeout it
+      // resynchronises with whatever was scored.
+      p.ready[2 * b + 1] = ok ? base + need : ld_acquire_gpu_u32(p.ready + 2 * b);
+      res[7] = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (!res[7]) L = 0;  // the wait gave up (reported): the row is written as all -1
+  }
+  // Score rows are read through L2 only (ld.global.cg): with ready counts the
+  // score grid may still be writing other rows, and each score is read once.
   const float* row = p.scores + static_cast<int64_t>(b) * p.score_stride;
   const unsigned int* ghist = p.hist + static_cast<int64_t>(b) * kBins;
   const int K = L < kTopK ? L : kTopK;
@@ -830,7 +875,7 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_select_kernel(const SelectPa
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     const int q = u * T + tid;
-    nv[u] = (L > kTopK && q < L4) ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+    nv[u] = (L > kTopK && q < L4) ? __ldcg(row4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int i = tid; i < kBins; i += T) hist2[i] = 0u;
   if (tid == 0) { res[3] = 0; res[4] = 0; res[5] = 0; }
@@ -838,7 +883,7 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_select_kernel(const SelectPa
   __syncthreads();
 
   if (L <= kTopK) {
-    for (int i = tid; i < kTopK; i += T) sel[i] = i < L ? composite(row[i], i) : 0ull;
+    for (int i = tid; i < kTopK; i += T) sel[i] = i < L ? composite(__ldcg(row + i), i) : 0ull;
     __syncthreads();
   } else {
     find_bin<T>(hist, K, warp_tot, res);
@@ -868,7 +913,7 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_select_kernel(const SelectPa
       for (int u = 0; u < 4; ++u) {
         v[u] = nv[u];
         const int q = q0 + (4 + u) * T + tid;
-        nv[u] = q < L4 ? row4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+        nv[u] = q < L4 ? __ldcg(row4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       uint32_t msk = 0;
 #pragma unroll
@@ -927,7 +972,7 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_select_kernel(const SelectPa
 #pragma unroll
         for (int u = 0; u < 4; ++u) ti[u] = j0 + 32 * u < avail ? static_cast<int>(mine[j0 + 32 * u]) : 0;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) sv[u] = j0 + 32 * u < avail ? __ldg(row + ti[u]) : 0.f;
+        for (int u = 0; u < 4; ++u) sv[u] = j0 + 32 * u < avail ? __ldcg(row + ti[u]) : 0.f;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           if (j0 + 32 * u < avail) {
@@ -960,7 +1005,7 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_select_kernel(const SelectPa
           }
         } else {
           for (int i = tid; i < L; i += T) {
-            const uint64_t c = composite(row[i], i);
+            const uint64_t c = composite(__ldcg(row + i), i);
             if ((c & mask) == prefix) atomicAdd(&hist[(c >> sh) & dm], 1u);
           }
         }
@@ -994,7 +1039,7 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_select_kernel(const SelectPa
       const int Lr = (L + 31) & ~31;
       for (int i = tid; i < Lr; i += T) {
         const bool in = i < L;
-        const uint64_t c = in ? composite(row[i], i) : 0ull;
+        const uint64_t c = in ? composite(__ldcg(row + i), i) : 0ull;
         warp_append(in && (c & mask) >= prefix, c, sel, &res[4], kTopK);
       }
     }
@@ -1029,8 +1074,8 @@ int g_sel_attr_status[64];
 
 int launch_topk_select(const float* scores, const unsigned int* hist, const int32_t* seq_lens,
                        const int32_t* block_table, const int32_t* row_req, int32_t* out, int rows,
-                       int score_stride, int max_pages, unsigned int* status, const DeviceInfo& info,
-                       cudaStream_t s) {
+                       int score_stride, int max_pages, unsigned int* status, unsigned int* ready,
+                       const DeviceInfo& info, cudaStream_t s) {
   if (ix::sel_smem<1024>() > info.max_smem_optin) return DSA_ERR_UNSUPPORTED_DEVICE;
   std::call_once(ix::g_sel_attr_once[info.device], [&]() {
     ix::g_sel_attr_status[info.device] =
@@ -1050,6 +1095,7 @@ int launch_topk_select(const float* scores, const unsigned int* hist, const int3
   selp.seq_lens = seq_lens;
   selp.block_table = block_table;
   selp.out = out;
+  selp.ready = ready;
   selp.score_stride = score_stride;
   selp.max_pages = max_pages;
   // One 1024-thread CTA per row while the rows fit the SMs in one wave (the
@@ -1071,7 +1117,7 @@ using namespace dsa;
 
 extern "C" size_t dsa_indexer_workspace_bytes(int32_t batch, int32_t max_pages) {
   if (batch < 0 || max_pages < 0) return 0;
-  return kWorkspaceHeader + sizeof(uint32_t) * static_cast<size_t>(batch) * ix::kBins +
+  return kWorkspaceHeader + ix::kReadyBytes + sizeof(uint32_t) * static_cast<size_t>(batch) * ix::kBins +
          sizeof(float) * static_cast<size_t>(batch) * static_cast<size_t>(max_pages) * ix::kPage;
 }
 
@@ -1125,7 +1171,7 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
     const int64_t n16 = static_cast<int64_t>(batch) * ix::kBins * 4 / 16;
     const int blocks = static_cast<int>(std::min<int64_t>((n16 + 255) / 256, info.num_sms));
     ix::hist_clear_kernel<<<blocks, 256, 0, s>>>(
-        reinterpret_cast<uint4*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeader), n16);
+        reinterpret_cast<uint4*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeader + ix::kReadyBytes), n16);
   }
   ix::ScoreParams sp;
   sp.k_cache = static_cast<const uint8_t*>(k_index_cache_fp8);
@@ -1133,8 +1179,9 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
   sp.seq_lens = seq_lens;
   sp.block_table = block_table;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  sp.hist = reinterpret_cast<unsigned int*>(ws + kWorkspaceHeader);
-  sp.scores = reinterpret_cast<float*>(ws + kWorkspaceHeader +
+  sp.ready = reinterpret_cast<unsigned int*>(ws + kWorkspaceHeader);
+  sp.hist = reinterpret_cast<unsigned int*>(ws + kWorkspaceHeader + ix::kReadyBytes);
+  sp.scores = reinterpret_cast<float*>(ws + kWorkspaceHeader + ix::kReadyBytes +
                                        sizeof(uint32_t) * static_cast<size_t>(batch) * ix::kBins);
   sp.status = static_cast<unsigned int*>(workspace);
   sp.num_pages = num_pages;
@@ -1146,5 +1193,5 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
     return DSA_ERR_CUDA;
 
   return launch_topk_select(sp.scores, sp.hist, seq_lens, block_table, nullptr, topk_indices, batch,
-                            sp.score_stride, max_pages, sp.status, info, s);
+                            sp.score_stride, max_pages, sp.status, sp.ready, info, s);
 }

@@ -163,6 +163,29 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   return v;
 }
 
+__device__ __forceinline__ unsigned int ld_acquire_gpu_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until the wrapping count *p has moved at least `need` past `base`
+// (unsigned difference).  Gives up after limit_ns, raising
+// DSA_DEV_WAIT_TIMEOUT; returns whether it did.
+__device__ __forceinline__ bool wait_count_since(const unsigned int* p, unsigned int base, unsigned int need,
+                                                 unsigned int* status, unsigned long long limit_ns) {
+  if (ld_acquire_gpu_u32(p) - base >= need) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (;;) {
+    __nanosleep(100);
+    if (ld_acquire_gpu_u32(p) - base >= need) return true;
+    if (global_timer_ns() - t0 > limit_ns) {
+      atomicOr(status, DSA_DEV_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // Waits until *p >= target.  Gives up after limit_ns, raising
 // DSA_DEV_WAIT_TIMEOUT; returns whether the value was reached.
 __device__ __forceinline__ bool wait_counter_at_least(const int* p, int target, unsigned int* status,

@@ -84,10 +84,14 @@ DSA_API int dsa_b200_abi_version(void);
 DSA_API const char* dsa_b200_status_string(int status);
 
 /* Bytes of device workspace dsa_indexer_run needs for this batch and block
- * table width: a 256-byte header, a [batch, 2048] uint32 radix histogram
- * (cleared by the call itself, on its stream, before the scores are added)
- * and [batch, max_pages*64] fp32 score rows.  Zero-fill a workspace once
- * before its first use so the status word in its header starts clear. */
+ * table width: a 256-byte header, 32 KiB of per-request ready counters
+ * (the score kernel counts each request's scored tiles there and the top-k
+ * select of that request starts once they are all counted; the counters
+ * carry over from call to call and are never reset), a [batch, 2048] uint32
+ * radix histogram (cleared by the call itself, on its stream, before the
+ * scores are added) and [batch, max_pages*64] fp32 score rows.  Zero-fill a
+ * workspace once before its first use, so that the status word in its
+ * header starts clear and the ready counters start consistent. */
 DSA_API size_t dsa_indexer_workspace_bytes(int32_t batch, int32_t max_pages);
 
 /* FP8 lightning indexer, decode (one query token per request).
@@ -149,9 +153,10 @@ DSA_API int dsa_attention_run(const void* q_nope, const void* q_pe,
                       void* workspace, size_t workspace_bytes, void* stream);
 
 /* Size of the scratch array compiled into the library for
- * dsa_indexer_run_noalloc: the 256-byte header, 64 radix histograms and
- * 1,048,576 fp32 score slots (4.5 MiB per GPU that loads the library). */
-#define DSA_NOALLOC_SCRATCH_BYTES (256u + 64u * 2048u * 4u + 1048576u * 4u)
+ * dsa_indexer_run_noalloc: the 256-byte header, the per-request ready
+ * counters (32 KiB), 64 radix histograms and 1,048,576 fp32 score slots
+ * (4.5 MiB per GPU that loads the library). */
+#define DSA_NOALLOC_SCRATCH_BYTES (256u + 32768u + 64u * 2048u * 4u + 1048576u * 4u)
 
 /* dsa_indexer_run without a workspace argument, for callers that cannot
  * allocate device memory when they call: hosts that reach this library

@@ -40,8 +40,8 @@ def test_version_and_status_strings():
 
 def test_workspace_sizes():
     lib = _native.lib()
-    assert lib.dsa_indexer_workspace_bytes(64, 1024) == 256 + 4 * 64 * 2048 + 4 * 64 * 1024 * 64
-    assert lib.dsa_indexer_workspace_bytes(0, 10) == 256
+    assert lib.dsa_indexer_workspace_bytes(64, 1024) == 256 + 32768 + 4 * 64 * 2048 + 4 * 64 * 1024 * 64
+    assert lib.dsa_indexer_workspace_bytes(0, 10) == 256 + 32768
     assert lib.dsa_attention_workspace_bytes(0) == 256
     assert lib.dsa_attention_workspace_bytes(8) > lib.dsa_attention_workspace_bytes(1)
 

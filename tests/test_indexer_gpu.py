@@ -174,7 +174,7 @@ def test_score_precision_vs_oracle(cuda_device):
     stream_id = torch.cuda.current_stream(cuda_device).cuda_stream
     buf = ws_mod.all_buffers()[(cuda_device.index, "indexer", stream_id)]
     stride = ix.block_table.shape[1] * 64
-    off = 256 + 2 * 2048 * 4   # header, then the per-request radix histograms
+    off = 256 + 32768 + 2 * 2048 * 4   # header, ready counters, then the radix histograms
     scores = buf[off:off + 4 * 2 * stride].view(torch.float32).reshape(2, stride).cpu()
     q, kc, w = ix.q_index_fp8.cpu(), ix.k_index_cache_fp8.cpu(), ix.weights.cpu()
     bt = ix.block_table.cpu()

@@ -50,8 +50,8 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(cuda_device)
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda_device):
     lib = _native.lib()
     limit = lib.dsa_indexer_workspace_bytes(64, 256)
-    assert limit <= (256 + 64 * 2048 * 4 + 1048576 * 4)
-    assert lib.dsa_indexer_workspace_bytes(64, 300) > (256 + 64 * 2048 * 4 + 1048576 * 4)
+    assert limit <= (256 + 32768 + 64 * 2048 * 4 + 1048576 * 4)
+    assert lib.dsa_indexer_workspace_bytes(64, 300) > (256 + 32768 + 64 * 2048 * 4 + 1048576 * 4)
     ix = workloads.make_indexer_inputs([64] * 64, pool_pages=300, seed=43, device=cuda_device,
                                        max_pages=300)
     out = torch.full((64, 2048), 7, dtype=torch.int32, device=cuda_device)
