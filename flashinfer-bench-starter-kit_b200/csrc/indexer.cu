@@ -147,14 +147,6 @@ __device__ __forceinline__ int clamp_len(int L, int max_len, unsigned int* statu
   return L;
 }
 
-__device__ __forceinline__ int page_id(const ScoreParams& p, int b, int page_idx) {
-  int pid = __ldg(p.block_table + static_cast<int64_t>(b) * p.max_pages + page_idx);
-  if (pid < 0 || pid >= p.num_pages) {
-    atomicOr(p.status, DSA_DEV_BAD_PAGE);
-    pid = 0;
-  }
-  return pid;
-}
 
 // Locates tile u of the work list: request b = the one with
 // tile_off[b] <= u < tile_off[b+1], tile j = u - tile_off[b].
@@ -175,16 +167,40 @@ struct TileInfo {
   int b, j, npg, p0, p1;
 };
 
+// Tile u's request, tile index and page ids in two steps: tile_info issues
+// the loads (the request's length and both block-table entries, independent
+// of each other, so one round trip) and uses none of their values;
+// finish_tile_info, called once the values are needed (a group of tiles
+// later in the producer), checks them and settles the page count.  The
+// producer thus never waits for the next group's loads before issuing the
+// current group's copies.
 __device__ __forceinline__ TileInfo tile_info(const ScoreParams& p, const int* tile_off,
-                                              int64_t u, int64_t u1, int max_len) {
+                                              int64_t u, int64_t u1) {
   TileInfo t{-1, 0, 0, 0, 0};
   if (u < u1) {
     locate(tile_off, p.batch, u, t.b, t.j);
-    const int L = clamp_len(__ldg(p.seq_lens + t.b), max_len, p.status);
+    const int32_t* row = p.block_table + static_cast<int64_t>(t.b) * p.max_pages;
+    t.npg = __ldg(p.seq_lens + t.b);  // the raw length until finish_tile_info
+    t.p0 = __ldg(row + 2 * t.j);
+    t.p1 = 2 * t.j + 1 < p.max_pages ? __ldg(row + 2 * t.j + 1) : 0;
+  }
+  return t;
+}
+__device__ __forceinline__ TileInfo finish_tile_info(const ScoreParams& p, TileInfo t, int max_len) {
+  if (t.b >= 0) {
+    const int L = clamp_len(t.npg, max_len, p.status);
     const int req_pages = (L + kPage - 1) / kPage;
     t.npg = (2 * t.j + 1 < req_pages) ? 2 : 1;
-    t.p0 = page_id(p, t.b, 2 * t.j);
-    t.p1 = t.npg == 2 ? page_id(p, t.b, 2 * t.j + 1) : 0;
+    if (t.p0 < 0 || t.p0 >= p.num_pages) {
+      atomicOr(p.status, DSA_DEV_BAD_PAGE);
+      t.p0 = 0;
+    }
+    if (t.npg == 1) {
+      t.p1 = 0;  // past the request's last page: the entry is not used or checked
+    } else if (t.p1 < 0 || t.p1 >= p.num_pages) {
+      atomicOr(p.status, DSA_DEV_BAD_PAGE);
+      t.p1 = 0;
+    }
   }
   return t;
 }
@@ -304,10 +320,10 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
     // n = k + kProdWarps * m, advanced incrementally.
     int s = k, sslot = k;
     uint32_t ph = 0;
-    TileInfo nxt = tile_info(p, tile_off, u0 + k + kProdWarps * lane, u1, max_len);
+    TileInfo nxt = tile_info(p, tile_off, u0 + k + kProdWarps * lane, u1);
     for (int g0 = 0; g0 < mine && ok; g0 += 32) {
-      info[lane] = nxt;
-      nxt = tile_info(p, tile_off, u0 + k + kProdWarps * (g0 + 32 + lane), u1, max_len);
+      info[lane] = finish_tile_info(p, nxt, max_len);
+      nxt = tile_info(p, tile_off, u0 + k + kProdWarps * (g0 + 32 + lane), u1);
       __syncwarp();
       const int cnt = mine - g0 < 32 ? mine - g0 : 32;
       if (lane == 0) {
