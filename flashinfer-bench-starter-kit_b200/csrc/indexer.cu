@@ -479,11 +479,16 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         }
         __syncwarp();
       };
-      // This warp's scored tiles of request fb count towards its ready count
-      // once its score stores and histogram flush are visible (release).
-      auto mark_ready = [&](int fb, int cnt) {
-        __threadfence();
-        __syncwarp();
+      // This warp's scored tiles of a request count towards its ready count
+      // once its score stores and histogram flush are visible (release: each
+      // lane's fence, then one lane's add).  A request left in mid-slice waits
+      // (pend_b, pend_cnt) and goes out behind the warp's next fence: the
+      // next request change or the final one.  A fence at every change would
+      // stall the epilogue for the acknowledgement of every store in flight,
+      // and the slice's first request is finished by the previous CTA at the
+      // end of its slice anyway.
+      int pend_b = -1, pend_cnt = 0;
+      auto add_ready = [&](int fb, int cnt) {
         if (lane == 0 && cnt > 0) atomicAdd(p.ready + 2 * fb, static_cast<unsigned int>(cnt));
       };
       enter();
@@ -540,7 +545,13 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         if (n + 2 < nt) {
           if ((j += 2) >= ntb) {
             flush(b);
-            mark_ready(b, scored);
+            if (pend_b >= 0) {  // a second request left in this slice
+              __threadfence();
+              __syncwarp();
+              add_ready(pend_b, pend_cnt);
+            }
+            pend_b = b;
+            pend_cnt = scored;
             scored = 0;
             since = 0;
             do { j -= ntb; ++b; ntb = tile_off[b + 1] - tile_off[b]; } while (j >= ntb);
@@ -552,7 +563,10 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         }
       }
       flush(b);
-      mark_ready(b, scored);
+      __threadfence();
+      __syncwarp();
+      if (pend_b >= 0) add_ready(pend_b, pend_cnt);
+      add_ready(b, scored);
     }
   }
 
