@@ -34,9 +34,10 @@
 //    radix select on the 64-bit key (order(score) << 32 | ~token), which
 //    encodes "score descending, then lower token index first" as one total
 //    order.  The score kernel's epilogue already histograms the top 11 key
-//    bits per request (per-warp shared-memory histograms flushed into a
-//    global [batch, 2048] table, cleared at each call by a small kernel that
-//    the score kernel overlaps through programmatic launch);
+//    bits per request (per-warp shared-memory histograms, summed by the
+//    CTA's eight epilogue warps together and added into a global
+//    [batch, 2048] table, cleared at each call by a small kernel that the
+//    score kernel overlaps through programmatic launch);
 //    one pass over the L scores then moves the winners of higher bins to the
 //    output and the boundary bin to a shared-memory candidate list, which
 //    later passes refine.  The 2048 winners are bucket-sorted on an 11-bit
@@ -78,9 +79,12 @@ constexpr int kMmaWarps = 4;
 constexpr int kThreads = 32 * (kMmaWarp0 + kMmaWarps);    // 14 warps
 constexpr int kBins = 2048;                               // radix bins: top 11 key bits
 // Each epilogue warp keeps its own histogram of 16-bit counters, two per
-// word, and flushes it at least every kFlushEvery of its tiles: 32 lanes x
-// 2047 tiles < 65536, so a counter never carries into its neighbour.
-constexpr int kFlushEvery = 2047;
+// word; the eight are flushed together at least every kFlushSpan slice
+// positions, i.e. every kFlushSpan / 2 tiles of a warp: 32 lanes x 128 tiles
+// < 65536, so a counter never carries into its neighbour.  (The span also
+// makes the periodic flush happen in slices of ordinary size.)
+constexpr int kFlushSpan = 256;
+static_assert(32 * (kFlushSpan / 2) < 65536, "16-bit histogram counters");
 constexpr int kMaxBatch = 4096;
 // Per-request ready counters at the front of the workspace, at fixed offsets
 // for every request index a call can have, so that a later call (of any
@@ -441,132 +445,160 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
       if (tid < nr) reinterpret_cast<int*>(smem + kOffLens)[tid] = __ldg(p.seq_lens + b_first + tid);
     }
     named_barrier_sync(1, 32 * kEpiWarps);
-    if (set < nt) {
-      int b = 0, j = 0;
-      locate(tile_off, p.batch, u0 + set, b, j);
-      int ntb = tile_off[b + 1] - tile_off[b];
-      int L = 0;
-      float* srow = nullptr;
-      float wt[kHeads];
-      auto enter = [&]() {  // request b becomes current
-        const bool staged = b - b_first < kWtReqs;
-        L = clamp_len(staged ? reinterpret_cast<const int*>(smem + kOffLens)[b - b_first] : __ldg(p.seq_lens + b),
-                      max_len, p.status);
-        srow = p.scores + static_cast<int64_t>(b) * p.score_stride;
-        if (staged) {
-          const float4* w4 = reinterpret_cast<const float4*>(w_smem + (b - b_first) * kHeads);
+    // Histogram flushes are done by the eight epilogue warps together: at a
+    // flush event they meet at a named barrier, each thread sums four words
+    // of the eight warps' shared-memory histograms (32-bit sums of the packed
+    // 16-bit counts) and adds the non-zero ones to the global histogram --
+    // at most 2048 global atomics per event instead of one per non-zero word
+    // of every warp (flushing separately measured 2.5 us per warp).  Events
+    // are positions of the slice: every request end inside it, every
+    // kFlushSpan positions (a warp scores at most kFlushSpan / 2 tiles
+    // between two flushes, so no 16-bit count overflows) and the slice end.  A warp
+    // flushes every event at or before its next tile's position before it
+    // scores that tile, and all remaining ones at the end, so all eight warps
+    // meet the same events in the same order, whatever tiles they hold or if
+    // they stopped early.
+    //
+    // A request's ready count (4 per tile scored in this slice) is added by
+    // one thread after every epilogue thread has fenced its score stores and
+    // histogram atomics (release).  A request finished in mid-slice waits
+    // for the next such fence (the next request end or the slice end): a
+    // fence at every end stalls the epilogue for the acknowledgement of
+    // every store in flight, and the slice's first request is finished by the
+    // previous CTA at the end of its slice anyway.  Nothing is added after an
+    // abort, so the select reports a timeout instead of reading a partial row.
+    if (nt > 0) {
+      int fpos = 0, fr = b_first, pend = -1;  // flushed up to position fpos; its request
+      auto cta_flush = [&](int r) {
+        named_barrier_sync(2, 32 * kEpiWarps);
+        unsigned int* g = p.hist + static_cast<int64_t>(r) * kBins;
+        for (int i = tid; i < kBins / 2; i += 32 * kEpiWarps) {
+          uint32_t lo = 0, hi = 0;
 #pragma unroll
-          for (int h = 0; h < kHeads / 4; ++h) {
-            const float4 x = w4[h];
-            wt[4 * h] = x.x; wt[4 * h + 1] = x.y; wt[4 * h + 2] = x.z; wt[4 * h + 3] = x.w;
+          for (int w = 0; w < kEpiWarps; ++w) {
+            const uint32_t x = hist_all[w * (kBins / 2) + i];
+            lo += x & 0xFFFFu;
+            hi += x >> 16;
+            hist_all[w * (kBins / 2) + i] = 0;
           }
-        } else {
-#pragma unroll
-          for (int h = 0; h < kHeads; ++h) wt[h] = __ldg(p.weights + b * kHeads + h);
+          if (lo) atomicAdd(g + 2 * i, lo);
+          if (hi) atomicAdd(g + 2 * i + 1, hi);
+        }
+        named_barrier_sync(2, 32 * kEpiWarps);
+      };
+      auto publish = [&](int r) {  // after a fence by every epilogue thread and a barrier
+        if (tid == 0 && !*static_cast<volatile int*>(abort_flag)) {
+          const int cnt = min(tile_off[r + 1], u1) - max(tile_off[r], u0);
+          if (cnt > 0) atomicAdd(p.ready + 2 * r, 4u * static_cast<unsigned int>(cnt));
         }
       };
-      // Adds the warp's counts (request fb) into the global histogram.
-      auto flush = [&](int fb) {
-        __syncwarp();
-        unsigned int* g = p.hist + static_cast<int64_t>(fb) * kBins;
-        for (int i = lane; i < kBins / 2; i += 32) {
-          const uint32_t w = hist[i];
-          if (w) {
-            if (w & 0xFFFFu) atomicAdd(g + 2 * i, w & 0xFFFFu);
-            if (w >> 16) atomicAdd(g + 2 * i + 1, w >> 16);
-            hist[i] = 0;
+      // Flushes every event at or before position P (the slice end included
+      // when P == nt).
+      auto flush_events = [&](int P) {
+        while (fpos < nt) {
+          const int er = tile_off[fr + 1] - u0;  // end of request fr in the slice
+          int e = min(er, nt);
+          e = min(e, (fpos / kFlushSpan + 1) * kFlushSpan);
+          if (e > P) break;
+          cta_flush(fr);
+          fpos = e;
+          if (e == nt) {
+            __threadfence();
+            named_barrier_sync(2, 32 * kEpiWarps);
+            if (pend >= 0) publish(pend);
+            publish(fr);
+          } else if (e == er) {
+            if (pend >= 0) {
+              __threadfence();
+              named_barrier_sync(2, 32 * kEpiWarps);
+              publish(pend);
+            }
+            pend = fr;
+            // The next request with tiles (position e < nt lies in one).
+            do { ++fr; } while (tile_off[fr + 1] == tile_off[fr]);
           }
         }
-        __syncwarp();
       };
-      // This warp's scored tiles of a request count towards its ready count
-      // once its score stores and histogram flush are visible (release: each
-      // lane's fence, then one lane's add).  A request left in mid-slice waits
-      // (pend_b, pend_cnt) and goes out behind the warp's next fence: the
-      // next request change or the final one.  A fence at every change would
-      // stall the epilogue for the acknowledgement of every store in flight,
-      // and the slice's first request is finished by the previous CTA at the
-      // end of its slice anyway.
-      int pend_b = -1, pend_cnt = 0;
-      auto add_ready = [&](int fb, int cnt) {
-        if (lane == 0 && cnt > 0) atomicAdd(p.ready + 2 * fb, static_cast<unsigned int>(cnt));
-      };
-      enter();
-      int a = set, slot = set, since = 0;  // accumulator, scale slot of tile n
-      int scored = 0;                       // tiles of request b this warp has scored
-      uint32_t aph = 0;
-      for (int n = set; n < nt; n += 2) {
-        const int tok = j * kTileTok + row;
-        if (!__all_sync(0xffffffffu, mbar_wait(&accfull[a], aph, wctx))) break;
-        tc_fence_after();
-        const float scale = *reinterpret_cast<const float*>(smem + kOffScale + slot * 2 * kScaleBytes + row * 4);
-        // relu(scale * v) = scale * relu(v) for scale > 0: one max
-        // (NaN-propagating, like the reference's v <= 0 ? 0 : v) and one fma
-        // per head; other scales (zero, negative, NaN) take relu(scale * v)
-        // term by term as the reference writes it.  Two 32-column halves keep
-        // the register footprint small enough for 14 warps.
-        const bool pos = scale > 0.f;
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + a * kHeads;
-        float f0 = 0.f, f1 = 0.f, g0 = 0.f;
-        float v[32];
+      if (set < nt) {
+        int b = 0, j = 0;
+        locate(tile_off, p.batch, u0 + set, b, j);
+        int ntb = tile_off[b + 1] - tile_off[b];
+        int L = 0;
+        float* srow = nullptr;
+        float wt[kHeads];
+        auto enter = [&]() {  // request b becomes current
+          const bool staged = b - b_first < kWtReqs;
+          L = clamp_len(staged ? reinterpret_cast<const int*>(smem + kOffLens)[b - b_first] : __ldg(p.seq_lens + b),
+                        max_len, p.status);
+          srow = p.scores + static_cast<int64_t>(b) * p.score_stride;
+          if (staged) {
+            const float4* w4 = reinterpret_cast<const float4*>(w_smem + (b - b_first) * kHeads);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          tmem_ld32_wait(taddr + 32 * half, v);
-          if (half == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&accempty[a]);
-          }
-          if (pos) {
-#pragma unroll
-            for (int h = 0; h < 32; h += 2) {
-              f0 = fmaf(relu_nan(v[h]), wt[32 * half + h], f0);
-              f1 = fmaf(relu_nan(v[h + 1]), wt[32 * half + h + 1], f1);
+            for (int h = 0; h < kHeads / 4; ++h) {
+              const float4 x = w4[h];
+              wt[4 * h] = x.x; wt[4 * h + 1] = x.y; wt[4 * h + 2] = x.z; wt[4 * h + 3] = x.w;
             }
           } else {
 #pragma unroll
-            for (int h = 0; h < 32; ++h) {
-              const float x = v[h] * scale;
-              g0 += (x <= 0.f ? 0.f : x) * wt[32 * half + h];
+            for (int h = 0; h < kHeads; ++h) wt[h] = __ldg(p.weights + b * kHeads + h);
+          }
+        };
+        enter();
+        int a = set, slot = set;  // accumulator, scale slot of tile n
+        uint32_t aph = 0;
+        for (int n = set; n < nt; n += 2) {
+          flush_events(n);
+          const int tok = j * kTileTok + row;
+          if (!__all_sync(0xffffffffu, mbar_wait(&accfull[a], aph, wctx))) break;
+          tc_fence_after();
+          const float scale = *reinterpret_cast<const float*>(smem + kOffScale + slot * 2 * kScaleBytes + row * 4);
+          // relu(scale * v) = scale * relu(v) for scale > 0: one max
+          // (NaN-propagating, like the reference's v <= 0 ? 0 : v) and one fma
+          // per head; other scales (zero, negative, NaN) take relu(scale * v)
+          // term by term as the reference writes it.  Two 32-column halves keep
+          // the register footprint small enough for 14 warps.
+          const bool pos = scale > 0.f;
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + a * kHeads;
+          float f0 = 0.f, f1 = 0.f, g0 = 0.f;
+          float v[32];
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            tmem_ld32_wait(taddr + 32 * half, v);
+            if (half == 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&accempty[a]);
+            }
+            if (pos) {
+#pragma unroll
+              for (int h = 0; h < 32; h += 2) {
+                f0 = fmaf(relu_nan(v[h]), wt[32 * half + h], f0);
+                f1 = fmaf(relu_nan(v[h + 1]), wt[32 * half + h + 1], f1);
+              }
+            } else {
+#pragma unroll
+              for (int h = 0; h < 32; ++h) {
+                const float x = v[h] * scale;
+                g0 += (x <= 0.f ? 0.f : x) * wt[32 * half + h];
+              }
             }
           }
-        }
-        if (tok < L) {
-          const float sc = pos ? scale * (f0 + f1) : g0;
-          srow[tok] = sc;
-          const uint32_t bin = score_key(sc) >> 21;
-          atomicAdd(&hist[bin >> 1], 1u << ((bin & 1u) << 4));
-        }
-        // Step to tile n + 2.
-        if ((a += 2) >= kAccStages) { a -= kAccStages; aph ^= 1; }
-        if ((slot += 2) >= kScaleSlots) slot -= kScaleSlots;
-        ++since;
-        ++scored;
-        if (n + 2 < nt) {
-          if ((j += 2) >= ntb) {
-            flush(b);
-            if (pend_b >= 0) {  // a second request left in this slice
-              __threadfence();
-              __syncwarp();
-              add_ready(pend_b, pend_cnt);
-            }
-            pend_b = b;
-            pend_cnt = scored;
-            scored = 0;
-            since = 0;
+          if (tok < L) {
+            const float sc = pos ? scale * (f0 + f1) : g0;
+            srow[tok] = sc;
+            const uint32_t bin = score_key(sc) >> 21;
+            atomicAdd(&hist[bin >> 1], 1u << ((bin & 1u) << 4));
+          }
+          // Step to tile n + 2.
+          if ((a += 2) >= kAccStages) { a -= kAccStages; aph ^= 1; }
+          if ((slot += 2) >= kScaleSlots) slot -= kScaleSlots;
+          if (n + 2 < nt && (j += 2) >= ntb) {
             do { j -= ntb; ++b; ntb = tile_off[b + 1] - tile_off[b]; } while (j >= ntb);
             enter();
-          } else if (since == kFlushEvery) {
-            flush(b);
-            since = 0;
           }
         }
       }
-      flush(b);
-      __threadfence();
-      __syncwarp();
-      if (pend_b >= 0) add_ready(pend_b, pend_cnt);
-      add_ready(b, scored);
+      flush_events(nt);
     }
   }
 
