@@ -15,10 +15,11 @@
 
 namespace {
 
-// The whole scratch of one indexer call: the 256-byte status header, one
-// 2048-bin radix histogram per request and the fp32 score rows.  Every GPU
-// that loads the library holds these bytes until the process exits; static
-// device memory starts zero-filled.
+// The whole scratch of one indexer call: the 256-byte status header, the
+// per-request ready counters, one 2048-bin radix histogram per request and
+// the fp32 score rows.  Every GPU that loads the library holds these bytes
+// until the process exits; static device memory starts zero-filled, which is
+// the state the ready counters must start from.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[DSA_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
@@ -52,9 +53,11 @@ extern "C" int dsa_indexer_run_noalloc(const void* q_index_fp8, const void* k_in
     if (e != cudaSuccess) cudaGetLastError();
   });
   if (g_scratch_status[dev] != DSA_OK) return g_scratch_status[dev];
-  // The histogram region is cleared inside dsa_indexer_run on every call and
-  // the score rows are rewritten for every token they are read at, so the
-  // previous call's contents need no clearing here.
+  // The histogram region is cleared inside dsa_indexer_run on every call,
+  // the score rows are rewritten for every token they are read at, and the
+  // ready counters (at fixed offsets for every request index) are left
+  // consistent by every call, so the previous call's contents need no
+  // clearing here.
   return dsa_indexer_run(q_index_fp8, k_index_cache_fp8, num_pages, weights, seq_lens,
                          block_table, batch, max_pages, topk_indices, g_scratch_ptr[dev],
                          DSA_NOALLOC_SCRATCH_BYTES, stream);
