@@ -246,8 +246,9 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int max_len = p.max_pages * kPage;
-  // The select kernel may start launching now: it waits for this grid's
-  // completion before it reads anything.
+  // The select kernel may start launching now: it reads a row's scores and
+  // histogram only once its request's ready count (released after the
+  // stores and atomics it covers) shows every tile of the request scored.
   griddep_launch_dependents();
 
   if (tid == 0) {
