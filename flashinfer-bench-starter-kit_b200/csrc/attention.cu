@@ -984,11 +984,17 @@ using namespace dsa;
 extern "C" int dsa_b200_test_inject(int kind, uint64_t wait_limit_ns) {
   if (kind == DSA_TEST_NONE) {
     attn::g_inject.store(0);
+    arm_indexer_test_fault(0);
     return DSA_OK;
   }
-  if (kind != DSA_TEST_SKIP_ARRIVAL || wait_limit_ns == 0 || wait_limit_ns >= (1ull << 56))
+  if ((kind != DSA_TEST_SKIP_ARRIVAL && kind != DSA_TEST_SKIP_READY) || wait_limit_ns == 0 ||
+      wait_limit_ns >= (1ull << 56))
     return DSA_ERR_INVALID_ARGUMENT;
-  attn::g_inject.store((static_cast<unsigned long long>(kind) << 56) | wait_limit_ns);
+  const unsigned long long armed = (static_cast<unsigned long long>(kind) << 56) | wait_limit_ns;
+  if (kind == DSA_TEST_SKIP_READY)
+    arm_indexer_test_fault(armed);  // consumed by the next dsa_indexer_run
+  else
+    attn::g_inject.store(armed);    // consumed by the next dsa_attention_run
   return DSA_OK;
 }
 

@@ -37,10 +37,16 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // each, programmatically after the kernel that wrote the scores): row b
 // reads scores[b], hist[b], seq_lens[b] and block-table row row_req[b]
 // (row_req == nullptr: row b; a negative entry yields an all -1 row).
+// With per-request ready counts (`ready`), a row's wait for them gives up
+// after wait_limit_ns.
 int launch_topk_select(const float* scores, const unsigned int* hist, const int32_t* seq_lens,
                        const int32_t* block_table, const int32_t* row_req, int32_t* out, int rows,
                        int score_stride, int max_pages, unsigned int* status, unsigned int* ready,
-                       const DeviceInfo& info, cudaStream_t s);
+                       unsigned long long wait_limit_ns, const DeviceInfo& info, cudaStream_t s);
+
+// Arms the indexer's test fault (dsa_b200_test_inject with DSA_TEST_SKIP_READY):
+// kind << 56 | wait limit in ns, or 0 to disarm.
+void arm_indexer_test_fault(unsigned long long armed);
 
 // Launches `kernel` on `stream` with programmatic stream serialization, so
 // its CTAs may be scheduled while the previous kernel on the stream drains

@@ -45,6 +45,7 @@
 //    keys crowd into few buckets) and translated to global slot ids through
 //    the block table (kernel.py:156-169), then -1 padded (kernel.py:206).
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "host.h"
@@ -139,6 +140,7 @@ struct ScoreParams {
   unsigned int* ready;
   int64_t num_pages;
   int batch;
+  int skip_ready_req;     // test hook: a request whose ready count is never published; -1 none
   int max_pages;
   int score_stride;       // = max_pages * 64
 };
@@ -488,7 +490,7 @@ indexer_score_kernel(const __grid_constant__ CUtensorMap kmap,
         named_barrier_sync(2, 32 * kEpiWarps);
       };
       auto publish = [&](int r) {  // after a fence by every epilogue thread and a barrier
-        if (tid == 0 && !*static_cast<volatile int*>(abort_flag)) {
+        if (tid == 0 && r != p.skip_ready_req && !*static_cast<volatile int*>(abort_flag)) {
           const int cnt = min(tile_off[r + 1], u1) - max(tile_off[r], u0);
           if (cnt > 0) atomicAdd(p.ready + 2 * r, 4u * static_cast<unsigned int>(cnt));
         }
@@ -635,6 +637,7 @@ struct SelectParams {
   // The score kernel's per-request ready counts ([2 b] scored, [2 b + 1]
   // consumed), or nullptr: wait for the whole score grid instead.
   unsigned int* ready;
+  unsigned long long wait_limit_ns;  // of the ready wait: kWaitLimitNs unless a test shortened it
   int score_stride;
   int max_pages;
 };
@@ -913,7 +916,7 @@ __global__ void __launch_bounds__(T, 1024 / T) topk_select_kernel(const SelectPa
       // Each of the request's tiles is scored by four epilogue warps.
       const unsigned int need = 4u * static_cast<unsigned int>((L + kTileTok - 1) / kTileTok);
       const unsigned int base = p.ready[2 * b + 1];
-      const bool ok = wait_count_since(p.ready + 2 * b, base, need, p.status, kWaitLimitNs);
+      const bool ok = wait_count_since(p.ready + 2 * b, base, need, p.status, p.wait_limit_ns);
       // The consumed count moves past this call's tiles; after a timeout it
       // resynchronises with whatever was scored.
       p.ready[2 * b + 1] = ok ? base + need : ld_acquire_gpu_u32(p.ready + 2 * b);
@@ -1133,12 +1136,19 @@ int g_attr_status[64];
 std::once_flag g_sel_attr_once[64];
 int g_sel_attr_status[64];
 
+// One armed test fault (dsa_b200_test_inject, kind DSA_TEST_SKIP_READY),
+// consumed by the next dsa_indexer_run: kind << 56 | the select's wait limit
+// in ns; 0 = none.
+std::atomic<unsigned long long> g_inject{0};
+
 }  // namespace ix
+
+void arm_indexer_test_fault(unsigned long long armed) { ix::g_inject.store(armed); }
 
 int launch_topk_select(const float* scores, const unsigned int* hist, const int32_t* seq_lens,
                        const int32_t* block_table, const int32_t* row_req, int32_t* out, int rows,
                        int score_stride, int max_pages, unsigned int* status, unsigned int* ready,
-                       const DeviceInfo& info, cudaStream_t s) {
+                       unsigned long long wait_limit_ns, const DeviceInfo& info, cudaStream_t s) {
   if (ix::sel_smem<1024>() > info.max_smem_optin) return DSA_ERR_UNSUPPORTED_DEVICE;
   std::call_once(ix::g_sel_attr_once[info.device], [&]() {
     ix::g_sel_attr_status[info.device] =
@@ -1159,6 +1169,7 @@ int launch_topk_select(const float* scores, const unsigned int* hist, const int3
   selp.block_table = block_table;
   selp.out = out;
   selp.ready = ready;
+  selp.wait_limit_ns = wait_limit_ns;
   selp.score_stride = score_stride;
   selp.max_pages = max_pages;
   // One 1024-thread CTA per row while the rows fit the SMs in one wave (the
@@ -1251,10 +1262,19 @@ extern "C" int dsa_indexer_run(const void* q_index_fp8, const void* k_index_cach
   sp.batch = batch;
   sp.max_pages = max_pages;
   sp.score_stride = max_pages * ix::kPage;
+  sp.skip_ready_req = -1;
+  unsigned long long wait_limit_ns = kWaitLimitNs;
+  if (ix::g_inject.load(std::memory_order_relaxed) != 0) {
+    const unsigned long long armed = ix::g_inject.exchange(0);
+    if ((armed >> 56) == DSA_TEST_SKIP_READY) {
+      sp.skip_ready_req = 0;
+      wait_limit_ns = armed & ((1ull << 56) - 1);
+    }
+  }
   if (launch_programmatic(ix::indexer_score_kernel, dim3(info.num_sms), dim3(ix::kThreads), smem1, s,
                           kmap, qmap, sp) != cudaSuccess)
     return DSA_ERR_CUDA;
 
   return launch_topk_select(sp.scores, sp.hist, seq_lens, block_table, nullptr, topk_indices, batch,
-                            sp.score_stride, max_pages, sp.status, sp.ready, info, s);
+                            sp.score_stride, max_pages, sp.status, sp.ready, wait_limit_ns, info, s);
 }

@@ -694,5 +694,5 @@ extern "C" int dsa_indexer_prefill_run(const void* q_index_fp8, const void* k_in
                           pf::kSmemBytes, s, kmap, qmap, sp) != cudaSuccess)
     return DSA_ERR_CUDA;
   return launch_topk_select(sp.scores, sp.hist, seq_lens, block_table, pp.row_req, topk_indices,
-                            num_rows, sp.score_stride, max_pages, sp.status, nullptr, info, s);
+                            num_rows, sp.score_stride, max_pages, sp.status, nullptr, kWaitLimitNs, info, s);
 }

@@ -49,6 +49,7 @@ SIGNATURES = {
 # dsa_b200_test_inject kinds (failure-path tests only)
 TEST_NONE = 0
 TEST_SKIP_ARRIVAL = 1
+TEST_SKIP_READY = 2
 
 _lib = None
 _lock = threading.Lock()

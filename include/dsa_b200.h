@@ -247,17 +247,26 @@ DSA_API int dsa_read_device_status(void* workspace, uint32_t* status_out, int cl
                            void* stream);
 
 /* ---- test hook ---------------------------------------------------------
- * Arms one fault for the next dsa_attention_run call made by any thread of
- * this process (the call consumes it): `kind` DSA_TEST_SKIP_ARRIVAL makes,
+ * Arms one fault for the next call of the operator it names, made by any
+ * thread of this process (the call consumes it).
+ * DSA_TEST_SKIP_ARRIVAL, for the next dsa_attention_run: makes,
  * in every CTA, the producers of its second tile issue no copy and no
  * arrival for it, and every bounded wait of that launch gives up after
  * `wait_limit_ns` instead of 2 s.  The launch then ends with
  * DSA_DEV_WAIT_TIMEOUT set and its output void; every wait stays bounded and
  * the workspace's merge counters are left at zero, so the next call is
- * exact.  kind DSA_TEST_NONE disarms.  For tests of the failure path only;
- * no counterpart in the reference. */
+ * exact.  kind DSA_TEST_NONE disarms every armed fault.  For tests of the
+ * failure path only; no counterpart in the reference. */
 #define DSA_TEST_NONE         0
 #define DSA_TEST_SKIP_ARRIVAL 1
+/* DSA_TEST_SKIP_READY, for the next dsa_indexer_run (the no-allocation entry
+ * point included): the score kernel publishes no ready count for request 0,
+ * and the select's wait for a request's ready count gives up after
+ * `wait_limit_ns` instead of 2 s.  The call ends with DSA_DEV_WAIT_TIMEOUT set
+ * and row 0 written as all -1; the other rows are exact, and the select
+ * resynchronises request 0's consumed count with its scored count, so the
+ * next call is exact. */
+#define DSA_TEST_SKIP_READY   2
 DSA_API int dsa_b200_test_inject(int kind, uint64_t wait_limit_ns);
 
 #ifdef __cplusplus

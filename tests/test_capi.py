@@ -94,7 +94,10 @@ def test_test_hook_validation():
     assert lib.dsa_b200_test_inject(7, 1000) == 1           # unknown kind
     assert lib.dsa_b200_test_inject(_native.TEST_SKIP_ARRIVAL, 0) == 1
     assert lib.dsa_b200_test_inject(_native.TEST_SKIP_ARRIVAL, 1000) == 0
-    assert lib.dsa_b200_test_inject(_native.TEST_NONE, 0) == 0  # disarm again
+    assert lib.dsa_b200_test_inject(_native.TEST_SKIP_READY, 0) == 1
+    assert lib.dsa_b200_test_inject(_native.TEST_SKIP_READY, 1 << 56) == 1
+    assert lib.dsa_b200_test_inject(_native.TEST_SKIP_READY, 1000) == 0
+    assert lib.dsa_b200_test_inject(_native.TEST_NONE, 0) == 0  # disarms both again
 
 
 def test_read_status_rejects_null():

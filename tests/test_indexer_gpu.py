@@ -246,3 +246,29 @@ def test_select_wide_and_narrow_ctas_agree(cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(narrow, wide[lo:hi]), (lo, hi)
     oracle_check(ix, wide, rows=[0, 1, 3, 7, n_sm + 2, n_sm + 5, B - 1])
+
+
+def test_ready_wait_timeout_is_reported_and_the_next_call_is_exact(cuda_device):
+    """Each request's select waits, bounded, until the score kernel has published
+    the request's ready count.  The failure path, made to happen without
+    faulting anything: a test hook makes the score kernel publish nothing for
+    request 0 and shortens the select's wait to 1 ms.  Request 0's select gives
+    up, reports DSA_DEV_WAIT_TIMEOUT and writes its row as all -1; the other
+    rows are exact.  The select then takes request 0's scored count as consumed,
+    so the next call on the same workspace is exact again."""
+    from dsa_b200 import _native
+    ix = workloads.make_indexer_inputs([70000, 3000, 65536, 129], pool_pages=1200, seed=97,
+                                       device=cuda_device)
+    good = run_gpu(ix).clone()
+    lib = _native.lib()
+    assert lib.dsa_b200_test_inject(_native.TEST_SKIP_READY, 1_000_000) == 0
+    out = torch.full_like(good, 7)
+    try:
+        with pytest.raises(DsaError, match="timed out"):
+            run_gpu(ix, out)
+    finally:
+        lib.dsa_b200_test_inject(_native.TEST_NONE, 0)
+    assert (out[0] == -1).all()
+    assert torch.equal(out[1:], good[1:])
+    for _ in range(2):
+        assert torch.equal(run_gpu(ix), good)
