@@ -3,22 +3,26 @@
 attention, one decode step per "step", on N GPUs of one node.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload north_star|config4]
+                    [--workload decode_64x65536|decode_512_mixed|prefill_4096|cache_write]
 
 For N > 1 launch under torchrun (one process per GPU).  The decode batch is
 sharded by request; every rank owns its own page pools and no collective runs
 inside the timed region (NCCL only gathers outputs for verification after it).
 
 Workloads (seeded synthetic data with the contest shapes):
-  north_star  64 requests per GPU, 65536-token context each (weak scaling).
-  config4     512 requests in total, context log-uniform in [4096, 131072],
-              split across the GPUs by context tokens (strong scaling).
-  config3     a prefill chunk: one request, 4096 query rows appended to a
-              61440-token prefix (causal), indexer rows scored as one FP8
-              GEMM, then attention for all 4096 rows; one replica per GPU.
-  cache_write the indexer K cache populated: 64 requests x 65536 tokens per GPU
-              (--batch / --seq-len override) quantised into the paged FP8
-              cache by dsa_index_cache_write, one launch per step.
+  decode_64x65536   64 requests per GPU, 65536-token context each (weak
+                    scaling); the default.
+  decode_512_mixed  512 requests in total, context log-uniform in [4096,
+                    131072], split across the GPUs by context tokens (strong
+                    scaling).
+  prefill_4096      a prefill chunk: one request, 4096 query rows appended to
+                    a 61440-token prefix (causal), indexer rows scored as one
+                    FP8 GEMM, then attention for all 4096 rows; one replica per
+                    GPU.
+  cache_write       the indexer K cache populated: 64 requests x 65536 tokens
+                    per GPU (--batch / --seq-len override) quantised into the
+                    paged FP8 cache by dsa_index_cache_write, one launch per
+                    step.
 
 Printed (rank 0, one JSON line): whole-job algorithmic HBM GB/s (value), the
 step time, the roofline of the dominant operator, the CPU oracle baseline,
@@ -54,15 +58,15 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["north_star", "config4", "config3", "cache_write"],
-                    default="north_star")
+    ap.add_argument("--workload", choices=["decode_64x65536", "decode_512_mixed", "prefill_4096", "cache_write"],
+                    default="decode_64x65536")
     ap.add_argument("--streams", type=int, default=1, help="streams inside the captured step")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-gpu-reference", action="store_true",
                     help="skip timing the reference's own GPU solutions (oracle/_ref)")
     ap.add_argument("--batch", type=int, default=0,
-                    help="requests per GPU (overrides the workload's batch; north_star shape)")
+                    help="requests per GPU (overrides the workload's batch; decode_64x65536 shape)")
     ap.add_argument("--seq-len", type=int, default=65536, help="context length with --batch")
     return ap.parse_args()
 
@@ -74,7 +78,7 @@ def workload_lengths(name: str, rank: int, world: int, batch: int = 0,
 
     if batch > 0:
         return [seq_len] * batch, batch * world, f"{batch} requests/GPU x {seq_len}-token context"
-    if name == "north_star":
+    if name == "decode_64x65536":
         return [65536] * 64, 64 * world, "64 requests/GPU x 65536-token context"
     g = torch.Generator().manual_seed(4)
     lens = workloads.log_uniform_lengths(512, 4096, 131072, g)
@@ -260,7 +264,7 @@ def run_reference(args, rank: int, world: int) -> int:
     line = {
         "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-        "scaling": "weak" if args.workload == "north_star" else "strong", "vs_baseline": None,
+        "scaling": "weak" if args.workload == "decode_64x65536" else "strong", "vs_baseline": None,
         "dtype": "fp32 (CPU oracle)", "data": "synthetic (seeded)", "impl": "reference",
         "config": {"workload": args.workload, "description": desc, "global_batch": total_req,
                    "l2": "inputs larger than L2"},
@@ -282,8 +286,8 @@ def main() -> int:
         return run_reference(args, rank, world)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.workload == "config3":
-        return run_config3(args, rank, world, local_rank)
+    if args.workload == "prefill_4096":
+        return run_prefill_chunk(args, rank, world, local_rank)
     if args.workload == "cache_write":
         return run_cache_write(args, rank, world, local_rank)
 
@@ -365,7 +369,9 @@ def main() -> int:
     peak, peak_kind = measured_peaks()
     ix_gbs = ix_bytes / (ix_ms * 1e-3) / 1e9
     at_gbs = at_bytes / (at_ms * 1e-3) / 1e9
-    traffic = profiled_traffic("indexer_op", args.workload)
+    # The profiled traffic is per launch of the workload's own shape; a --batch
+    # override runs another shape, which has no profiled figure.
+    traffic = profiled_traffic("indexer_op", args.workload) if args.batch == 0 else None
     cpu = None
     if world == 1 and args.cpu_seconds > 0:
         cpu = cpu_oracle_sample(dec, step.topk, args.cpu_seconds)
@@ -376,7 +382,7 @@ def main() -> int:
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,
         "tokens_per_s": n_req / (ms_step * 1e-3), "higher_is_better": True,
-        "scaling": "weak" if args.workload == "north_star" else "strong", "vs_baseline": None,
+        "scaling": "weak" if args.workload == "decode_64x65536" else "strong", "vs_baseline": None,
         "dtype": "fp8e4m3 (indexer MMA) + bf16 (attention MMA), fp32 accumulate",
         "data": "synthetic (seeded N(0,1), contest shapes)",
         "config": {"workload": args.workload, "description": desc, "global_batch": total_req,
@@ -569,7 +575,7 @@ def fp8_gemm_peak(dev, n: int = 8192, reps: int = 10) -> float:
     return 2.0 * n ** 3 / (best * 1e-3) / 1e12
 
 
-def run_config3(args, rank: int, world: int, local_rank: int) -> int:
+def run_prefill_chunk(args, rank: int, world: int, local_rank: int) -> int:
     """Prefill chunk: indexer.run_prefill over 4096 causal rows of one request
     (61441 .. 65536 tokens each), then attention.run for the 4096 rows, one
     CUDA graph per step.  Each GPU runs its own replica (the chunk does not
@@ -700,7 +706,7 @@ def run_config3(args, rank: int, world: int, local_rank: int) -> int:
         "scaling": "weak", "vs_baseline": None,
         "dtype": "fp8e4m3 (indexer MMA) + bf16 (attention MMA), fp32 accumulate",
         "data": "synthetic (seeded N(0,1), contest shapes)",
-        "config": {"workload": "config3",
+        "config": {"workload": "prefill_4096",
                    "description": "prefill chunk: 4096 causal query rows on a 61440-token prefix "
                                   "(rows see 61441..65536 tokens)",
                    "rows_per_gpu": T, "parallelism": f"{world} replicas",
@@ -879,7 +885,8 @@ def run_cache_write(args, rank: int, world: int, local_rank: int) -> int:
         "roofline": {"bound": "hbm", "op": "index K-cache writer", "achieved": per_gpu,
                      "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
-                     "traffic": profiled_traffic("index_cache_write_kernel", "cache_write")},
+                     "traffic": (profiled_traffic("index_cache_write_kernel", "cache_write")
+                                 if args.batch == 0 and args.seq_len == 65536 else None)},
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": K,

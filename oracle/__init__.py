@@ -15,8 +15,8 @@ lightning indexer and the DSA sparse MLA attention:
                           attention.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
-``bench.py`` may import this package, and only as the checker / the timed CPU
-baseline.  The product path (``dsa_b200``) never imports it and has no CPU
+``bench.py`` may import this package, and only to check results against it or as the
+timed CPU baseline.  The product path (``dsa_b200``) never imports it and has no CPU
 fallback.
 
 Parity pinning: the attention restatement and the top-k/page-table step are

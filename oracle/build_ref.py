@@ -16,12 +16,12 @@ nothing on import) and compiles them with the same ``load_inline`` call, the
 same module names, functions and flags, for compute capability 10.0 -- the
 target the reference's JIT picks on a B200, since it passes no architecture
 flag.  Only the two extension libraries are kept (``oracle/_ref/*.so``,
-git-ignored, shipped to the GPU box with the tree); the generated build
+git-ignored, travelling with a copy of the source tree); the generated build
 folders, which hold the sources, are deleted.  Nothing under /root/reference
 is written.
 
-The libraries are used by ``oracle.ref_gpu`` as a second parity checker (the
-reference itself, run on the GPU) and as the same-box GPU baseline.
+The libraries are used by ``oracle.ref_gpu`` for a second parity check (against
+the reference itself, run on the GPU) and as the same-box GPU baseline.
 """
 
 from __future__ import annotations
@@ -63,8 +63,8 @@ def stale(name: str) -> bool:
 
 def build(force: bool = False, verbose: bool = False) -> list:
     """Builds every target that is missing or older than its source; returns
-    the library paths.  Without /root/reference (the GPU box) it only
-    reports what is already built."""
+    the library paths.  Where /root/reference is absent it only reports what
+    is already built."""
     if not REF_ROOT.exists():
         return sorted(OUT.glob("*.so"))
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0"

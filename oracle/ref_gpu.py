@@ -3,7 +3,7 @@
 ``oracle/build_ref.py`` compiles the reference's inline CUDA/C++ sources,
 unmodified, into ``oracle/_ref/dsa_topk_s11.so`` and ``dsa_sparse_v8.so``.
 This module loads them and restates the two Python ``run()`` wrappers around
-them, so that the reference's stock code path can serve as a parity checker
+them, so that the reference's stock code path can serve for a parity check
 and as the same-box GPU baseline:
 
 * ``RefIndexer.run`` follows dsa_indexer/solution/triton/kernel.py:364-436:

@@ -52,7 +52,7 @@ def test_small_batches(cuda_device, T):
     print(f"T={T}: out max_abs {ro.max_abs:.3g}, lse max_abs {rl.max_abs:.3g}")
 
 
-def test_config1_batch8(cuda_device):
+def test_eight_tokens(cuda_device):
     a = workloads.make_attention_inputs(8, pool_pages=2048, seed=1, device=cuda_device)
     out, lse = run_gpu(a)
     check(a, out, lse)

@@ -53,13 +53,13 @@ def test_small_lengths(cuda_device, seq_lens):
     assert rep.swaps == 0
 
 
-def test_config0_batch8(cuda_device):
+def test_eight_requests_2k_to_8k(cuda_device):
     g = torch.Generator().manual_seed(0)
     lens = workloads.uniform_lengths(8, 2048, 8192, g)
     ix = workloads.make_indexer_inputs(lens, pool_pages=1024, seed=0, device=cuda_device)
     got = run_gpu(ix)
     rep = oracle_check(ix, got)
-    print(f"config0: exact rows {rep.exact_rows}/8, boundary swaps {rep.swaps}")
+    print(f"8 requests of 2048-8192 tokens: exact rows {rep.exact_rows}/8, boundary swaps {rep.swaps}")
 
 
 def test_golden_fixture(cuda_device):
@@ -189,7 +189,7 @@ def test_score_precision_vs_oracle(cuda_device):
     assert worst <= 1.0
 
 
-def test_long_context_config2(cuda_device):
+def test_64_requests_32k_to_128k(cuda_device):
     g = torch.Generator().manual_seed(2)
     lens = workloads.uniform_lengths(64, 32768, 131072, g)
     ix = workloads.make_indexer_inputs(lens, pool_pages=150_000, seed=2, device=cuda_device)
@@ -203,7 +203,7 @@ def test_long_context_config2(cuda_device):
         assert (row >= 0).all() and row.unique().numel() == 2048, b
         pages = set(bt[b, : (lens[b] + 63) // 64].tolist())
         assert set((row // 64).tolist()) <= pages, b
-    print(f"config2 sample: exact {rep.exact_rows}/3, swaps {rep.swaps}")
+    print(f"64 requests of 32768-131072 tokens, sampled: exact {rep.exact_rows}/3, swaps {rep.swaps}")
 
 
 def test_workspace_reuse_across_sizes(cuda_device):

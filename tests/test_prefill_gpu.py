@@ -94,14 +94,14 @@ def test_prefill_equals_decode_kernel(cuda_device):
     assert float(same.float().mean()) >= 0.9
 
 
-def test_prefill_config3_sampled_rows(cuda_device):
+def test_prefill_4096_rows_sampled(cuda_device):
     # One request, 4096 query rows appended to a 61440-token prefix (rows of
     # length 61441 .. 65536): sampled rows against the oracle.
     pf = workloads.make_prefill_inputs([61440], [4096], seed=3, device=cuda_device)
     got = run_prefill(pf)
     rows = [0, 1, 2, 3, 1000, 2047, 4094, 4095]
     rep = oracle_check(pf, got, rows)
-    print(f"config3 sampled rows: exact {rep.exact_rows}/{len(rows)}, swaps {rep.swaps}")
+    print(f"prefill, 4096 rows, sampled: exact {rep.exact_rows}/{len(rows)}, swaps {rep.swaps}")
 
 
 def test_prefill_repeated_calls_and_graph(cuda_device):

@@ -84,12 +84,12 @@ def compare_with_reference(ix, ours, theirs):
     return same, swaps
 
 
-def test_indexer_config0_vs_reference(cuda_device, ref_indexer):
+def test_indexer_8_requests_2k_to_8k_vs_reference(cuda_device, ref_indexer):
     g = torch.Generator().manual_seed(0)
     lens = workloads.uniform_lengths(8, 2048, 8192, g)
     ix = workloads.make_indexer_inputs(lens, pool_pages=1024, seed=0, device=cuda_device)
     same, swaps = compare_with_reference(ix, ours_indexer(ix), reference_indexer(ref_indexer, ix))
-    print(f"config 0 vs reference: {same}/8 rows identical as sets, {swaps} boundary swaps")
+    print(f"8 requests of 2048-8192 tokens vs reference: {same}/8 rows identical as sets, {swaps} boundary swaps")
 
 
 def test_indexer_short_rows_vs_reference(cuda_device, ref_indexer):
@@ -102,12 +102,12 @@ def test_indexer_short_rows_vs_reference(cuda_device, ref_indexer):
     assert (ours[3] == -1).all() and (theirs[3] == -1).all()
 
 
-def test_indexer_config2_vs_reference(cuda_device, ref_indexer):
+def test_indexer_64_requests_32k_to_128k_vs_reference(cuda_device, ref_indexer):
     g = torch.Generator().manual_seed(2)
     lens = workloads.uniform_lengths(64, 32768, 131072, g)
     ix = workloads.make_indexer_inputs(lens, pool_pages=150000, seed=2, device=cuda_device)
     same, swaps = compare_with_reference(ix, ours_indexer(ix), reference_indexer(ref_indexer, ix, calls=4))
-    print(f"config 2 vs reference: {same}/64 rows identical as sets, {swaps} boundary swaps")
+    print(f"64 requests of 32768-131072 tokens vs reference: {same}/64 rows identical as sets, {swaps} boundary swaps")
 
 
 def _attention_pair(a):
@@ -123,8 +123,8 @@ def _attention_pair(a):
     return out.cpu(), lse.cpu(), rout.cpu(), rlse.cpu()
 
 
-def test_attention_config1_vs_reference(cuda_device, ref_indexer):
-    # Config 1 plus rows with 1, 100 and 2047 valid indices (the rest -1).
+def test_attention_eleven_tokens_vs_reference(cuda_device, ref_indexer):
+    # Eight tokens of 2048 valid indices plus tokens with 1, 100 and 2047 (the rest -1).
     a = workloads.make_attention_inputs(11, pool_pages=2048, seed=1, device=cuda_device,
                                         valid_counts=[2048] * 8 + [1, 100, 2047])
     out, lse, rout, rlse = _attention_pair(a)
@@ -132,12 +132,12 @@ def test_attention_config1_vs_reference(cuda_device, ref_indexer):
     rl = compare.harness_close(lse, rlse, LSE_TOL, LSE_TOL)
     assert ro.ok, f"output: {ro}"
     assert rl.ok, f"lse: {rl}"
-    print(f"config 1 vs reference: output max_abs {ro.max_abs:.3g} max_rel {ro.max_rel:.3g}; "
+    print(f"11 tokens vs reference: output max_abs {ro.max_abs:.3g} max_rel {ro.max_rel:.3g}; "
           f"lse max_abs {rl.max_abs:.3g}")
 
 
-def test_decode_step_north_star_vs_reference(cuda_device, ref_indexer):
-    """The north-star step (64 requests x 65536 tokens): the whole indexer
+def test_decode_step_64x65536_vs_reference(cuda_device, ref_indexer):
+    """The decode step of 64 requests x 65536 tokens: the whole indexer
     output against the reference's, and attention over this library's
     selections against the reference's attention over the same selections."""
     dec = workloads.make_decode_inputs([65536] * 64, seed=1000, device=cuda_device)
@@ -156,6 +156,6 @@ def test_decode_step_north_star_vs_reference(cuda_device, ref_indexer):
     rl = compare.harness_close(step.lse.cpu(), rlse.cpu(), LSE_TOL, LSE_TOL)
     assert ro.ok, f"output: {ro}"
     assert rl.ok, f"lse: {rl}"
-    print(f"north star vs reference: {same}/64 indexer rows identical as sets, {swaps} boundary "
+    print(f"64 x 65536 decode step vs reference: {same}/64 indexer rows identical as sets, {swaps} boundary "
           f"swaps; attention output max_abs {ro.max_abs:.3g} max_rel {ro.max_rel:.3g}, "
           f"lse max_abs {rl.max_abs:.3g}")
