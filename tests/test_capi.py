@@ -24,6 +24,13 @@ def test_header_declares_the_abi():
     assert set(names) == set(_native.SIGNATURES), names
 
 
+def test_test_hook_kinds_match_the_header():
+    kinds = dict(re.findall(r"^#define\s+DSA_TEST_(\w+)\s+(\d+)", HEADER.read_text(), re.M))
+    assert {k: int(v) for k, v in kinds.items()} == {
+        "NONE": _native.TEST_NONE, "SKIP_ARRIVAL": _native.TEST_SKIP_ARRIVAL,
+        "SKIP_READY": _native.TEST_SKIP_READY}
+
+
 def test_library_exports_every_declared_symbol():
     lib = _native.lib()
     for name in declared_functions():
