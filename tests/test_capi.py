@@ -24,6 +24,17 @@ def test_header_declares_the_abi():
     assert set(names) == set(_native.SIGNATURES), names
 
 
+def test_device_status_bits_match_the_header():
+    bits = dict(re.findall(r"^#define\s+DSA_DEV_(\w+)\s+(0x[0-9a-fA-F]+)u", HEADER.read_text(), re.M))
+    assert {k: int(v, 16) for k, v in bits.items()} == {
+        "BAD_SEQ_LEN": _native.DEV_BAD_SEQ_LEN, "BAD_PAGE": _native.DEV_BAD_PAGE,
+        "BAD_INDEX": _native.DEV_BAD_INDEX, "WAIT_TIMEOUT": _native.DEV_WAIT_TIMEOUT,
+        "STALE_WORKSPACE": _native.DEV_STALE_WORKSPACE}
+    # Every bit has its own message.
+    for b in bits.values():
+        assert _native.describe_device_status(int(b, 16)), b
+
+
 def test_test_hook_kinds_match_the_header():
     kinds = dict(re.findall(r"^#define\s+DSA_TEST_(\w+)\s+(\d+)", HEADER.read_text(), re.M))
     assert {k: int(v) for k, v in kinds.items()} == {
