@@ -24,6 +24,14 @@ def test_header_declares_the_abi():
     assert set(names) == set(_native.SIGNATURES), names
 
 
+def test_every_return_code_has_its_own_message():
+    codes = dict(re.findall(r"^#define\s+(DSA_(?:OK|ERR_\w+))\s+(\d+)", HEADER.read_text(), re.M))
+    assert int(codes.pop("DSA_OK")) == _native.DSA_OK == 0
+    lib = _native.lib()
+    msgs = {lib.dsa_b200_status_string(int(v)) for v in codes.values()}
+    assert len(msgs) == len(codes) and b"unknown status" not in msgs, msgs
+
+
 def test_device_status_bits_match_the_header():
     bits = dict(re.findall(r"^#define\s+DSA_DEV_(\w+)\s+(0x[0-9a-fA-F]+)u", HEADER.read_text(), re.M))
     assert {k: int(v, 16) for k, v in bits.items()} == {
